@@ -1,0 +1,259 @@
+/*
+ * b200k.h — C ABI of libb200k.so, the sm_100a (B200) kernel library behind the
+ * torch.compile backend in torch-compile-backend_b200/compiler.
+ *
+ * Plain C: device pointers, int64 sizes/strides (in ELEMENTS, not bytes), dtype
+ * enums and a small epilogue program.  No torch or CUDA types appear in the
+ * signatures; `stream` is a cudaStream_t passed as void* (NULL = legacy default
+ * stream).  The library never allocates or frees device memory: outputs are
+ * allocated by the caller.  Every entry point returns B200K_OK (0) or an error
+ * code; b200k_status_string() turns it into text.  Errors detected on the host
+ * (shapes, alignment, unsupported dtypes, launch failure) are returned
+ * immediately; a device-side wait that runs out of time is reported through the
+ * optional `status` word of the GEMM arguments (read it after synchronising).
+ *
+ * Reference interfaces replaced (aashrith-madasu/torch-compile-backend):
+ *   b200k_pointwise      <- the generated `fused_<n>` Triton kernel and its launch
+ *                           closure `fused_op(*tensors)`
+ *                           compiler/optimization/fusion_pointwise.py:155-192,212-233
+ *   b200k_gemm_epilogue  <- the generated autotuned `gemm_epilogue_<n>` Triton kernel
+ *                           and its closure `epilogue_op(a, b, *tensors)`
+ *                           compiler/optimization/fusion_epilogue.py:72-180; also the
+ *                           standalone demos hand_written/gemm_kernel.py:6-71 and
+ *                           hand_written/gemm_swizzled_kernel.py:5-89
+ *   b200k_pointwise (ADD program) <- hand_written/matrix_add_kernel.py:6-46
+ *   b200k_rownorm, b200k_softmax  <- no Triton counterpart: the reference leaves
+ *                           pow/mean/native_layer_norm/_softmax to ATen
+ *                           (compiler/optimization/fusion_pointwise.py:35-53 has no
+ *                           reduction entries); these fuse the whole row group.
+ */
+#ifndef B200K_H
+#define B200K_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B200K_MAX_DIMS 6
+#define B200K_MAX_INPUTS 8
+#define B200K_MAX_SLOTS 8
+#define B200K_MAX_INSTR 64
+
+/* Element types. */
+enum {
+  B200K_F32 = 0,
+  B200K_F16 = 1,
+  B200K_BF16 = 2,
+  B200K_F64 = 3,
+  B200K_I32 = 4,
+  B200K_I64 = 5,
+  B200K_BOOL = 6,
+  B200K_U8 = 7
+};
+
+/* Return codes. */
+enum {
+  B200K_OK = 0,
+  B200K_ERR_ARG = 1,         /* null pointer, negative size, bad enum */
+  B200K_ERR_ALIGN = 2,       /* pointer/stride alignment the kernel needs is not met */
+  B200K_ERR_SHAPE = 3,       /* inconsistent or too large shape */
+  B200K_ERR_UNSUPPORTED = 4, /* dtype/layout combination not implemented */
+  B200K_ERR_LAUNCH = 5,      /* CUDA launch or attribute error */
+  B200K_ERR_TIMEOUT = 6,     /* a device-side wait ran out of time (status word) */
+  B200K_ERR_PROGRAM = 7,     /* malformed epilogue program */
+  B200K_ERR_DEVICE = 8       /* no sm_100 device current */
+};
+
+/*
+ * Epilogue / pointwise program: an accumulator machine evaluated per element in
+ * fp32.  State: one accumulator `acc` and B200K_MAX_SLOTS value slots.  Before
+ * the first instruction the slots hold the operands:
+ *   b200k_pointwise:     slot i = inputs[i]             (i < n_inputs)
+ *   b200k_gemm_epilogue: slot 0 = A·B accumulator, slot i = extras[i-1]
+ * Instruction word: code = op * 10 + operand, operand 0..7 = slot, 8 = imm,
+ * 9 = none.  Binary ops compute acc = acc (op) x; R* ops swap the operands.
+ * After the last instruction `acc` is rounded to the output dtype and stored.
+ * Op semantics follow compiler/optimization/fusion_pointwise.py:35-53 (fp32
+ * math; tanh is 2*sigmoid(2x)-1; sigmoid is 1/(1+exp(-x)); relu/max/min return
+ * the non-NaN operand).  ROUND_* are for fusions that cross a sub-fp32 cast.
+ */
+enum {
+  B200K_OP_NOP = 0,
+  B200K_OP_MOV = 1,    /* acc = x                    */
+  B200K_OP_STORE = 2,  /* slot[operand] = acc        */
+  B200K_OP_ADD = 3,
+  B200K_OP_SUB = 4,    /* acc = acc - x              */
+  B200K_OP_RSUB = 5,   /* acc = x - acc              */
+  B200K_OP_MUL = 6,
+  B200K_OP_DIV = 7,    /* acc = acc / x              */
+  B200K_OP_RDIV = 8,   /* acc = x / acc              */
+  B200K_OP_MAX = 9,
+  B200K_OP_MIN = 10,
+  B200K_OP_NEG = 11,
+  B200K_OP_ABS = 12,
+  B200K_OP_RELU = 13,
+  B200K_OP_EXP = 14,
+  B200K_OP_LOG = 15,
+  B200K_OP_SQRT = 16,
+  B200K_OP_RSQRT = 17,
+  B200K_OP_ERF = 18,
+  B200K_OP_SIGMOID = 19,
+  B200K_OP_TANH = 20,
+  B200K_OP_ROUND_BF16 = 21,
+  B200K_OP_ROUND_F16 = 22,
+  B200K_OP_COUNT = 23
+};
+#define B200K_OPERAND_IMM 8
+#define B200K_OPERAND_NONE 9
+
+typedef struct {
+  int32_t code; /* op * 10 + operand */
+  float imm;    /* used when operand == B200K_OPERAND_IMM */
+} B200kInstr;
+
+typedef struct {
+  int32_t n;
+  int32_t pad;
+  B200kInstr ins[B200K_MAX_INSTR];
+} B200kProgram;
+
+/* A strided view broadcast to the output shape (stride 0 on broadcast dims). */
+typedef struct {
+  const void* ptr;
+  int32_t dtype;
+  int32_t pad;
+  int64_t strides[B200K_MAX_DIMS];
+} B200kTensorRef;
+
+/*
+ * out[i0..i_{r-1}] = program(inputs at the same index), out contiguous.
+ * Replaces fusion_pointwise.py:155-192 (generated kernel) + :224-230 (launch).
+ */
+typedef struct {
+  int32_t rank; /* 0..B200K_MAX_DIMS */
+  int32_t n_inputs;
+  int64_t sizes[B200K_MAX_DIMS];
+  B200kTensorRef inputs[B200K_MAX_INPUTS];
+  void* out;
+  int32_t out_dtype;
+  int32_t pad;
+  B200kProgram program;
+} B200kPointwiseArgs;
+
+int b200k_pointwise(const B200kPointwiseArgs* args, void* stream);
+
+/* An epilogue operand indexed by the output coordinate (m, n). */
+typedef struct {
+  const void* ptr;
+  int32_t dtype;
+  int32_t pad;
+  int64_t stride_m;
+  int64_t stride_n;
+} B200kEpiOperand;
+
+/*
+ * out[m,n] = program(acc[m,n], extras[..][m,n]) with acc = sum_k a[m,k]*b[k,n]
+ * accumulated in fp32 on the tcgen05 tensor cores.  a is [M,K] with unit K
+ * stride; b is the reference's mat2 [K,N] (usually t(W) with unit K stride,
+ * "K-major"; unit N stride, "N-major", is also accepted).  a/b dtype: f16 or
+ * bf16.  out: f16, bf16 or f32 with unit N stride.
+ * Replaces fusion_epilogue.py:72-151 (kernel), :164-177 (launch) and the
+ * AUTOTUNE_CONFIGS table (:31-38) with a fixed B200 tile table.
+ */
+typedef struct {
+  int64_t M, N, K;
+  const void* a;
+  int64_t a_stride_m, a_stride_k;
+  const void* b;
+  int64_t b_stride_k, b_stride_n;
+  int32_t ab_dtype;
+  int32_t out_dtype;
+  void* out;
+  int64_t out_stride_m, out_stride_n;
+  int32_t n_extras;
+  int32_t tile_config; /* -1 = pick from the built-in table */
+  B200kEpiOperand extras[B200K_MAX_INPUTS - 1];
+  B200kProgram program;
+  int32_t* status;     /* optional device word: set to B200K_ERR_TIMEOUT by a stuck wait */
+  int64_t timeout_ns;  /* 0 = default (2 s) */
+} B200kGemmArgs;
+
+int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
+
+/* Number of GEMM tile configurations in the built-in table and their shapes. */
+int b200k_gemm_num_configs(void);
+int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages);
+/* The configuration b200k_gemm_epilogue picks for a problem when tile_config is -1. */
+int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K);
+
+/*
+ * Row normalisation over the last dim of a [rows, cols] view (unit column
+ * stride), fp32 statistics.  No reference counterpart (the reference leaves
+ * pow/mean/rsqrt partly to ATen and native_layer_norm wholly to ATen).
+ *   RMSNORM:        n = x * rsqrt(mean(x^2) + eps)
+ *   LAYERNORM:      n = (x - mean) * rsqrt(var + eps)          (biased var)
+ *   RMSNORM_SWIGLU: n as RMSNORM over the full row, then
+ *                   out[:, j] = silu(g_j) * u_j, g = y[:, :cols/2], u = y[:, cols/2:]
+ * with y = affine(n) and the rounding points given by `flags`, so that the
+ * kernel reproduces eager PyTorch's bf16/f16 rounding of the decomposed graph.
+ */
+enum {
+  B200K_ROW_RMSNORM = 0,
+  B200K_ROW_LAYERNORM = 1,
+  B200K_ROW_RMSNORM_SWIGLU = 2
+};
+enum {
+  B200K_ROWF_ROUND_NORMED = 1,  /* round n to x's dtype before the weight multiply */
+  B200K_ROWF_ROUND_AFFINE = 2,  /* round y = n*w (+b) to the output dtype (affine done in low precision) */
+  B200K_ROWF_ROUND_SILU = 4,    /* round silu(g) to the output dtype before multiplying by u */
+  B200K_ROWF_WEIGHT_PLUS_ONE = 8 /* use (1 + w) as the scale (Gemma-style) */
+};
+
+typedef struct {
+  int64_t rows, cols;
+  const void* x;
+  int64_t x_row_stride;
+  int32_t x_dtype;
+  int32_t kind;
+  const void* weight; /* [cols] or NULL */
+  int32_t w_dtype;
+  int32_t flags;
+  const void* bias;   /* [cols] or NULL (LAYERNORM only) */
+  int32_t b_dtype;
+  float eps;
+  void* out;
+  int64_t out_row_stride;
+  int32_t out_dtype;
+  int32_t pad;
+  float* mean_out;    /* [rows] fp32 or NULL (LAYERNORM) */
+  float* rstd_out;    /* [rows] fp32 or NULL (RMSNORM, LAYERNORM) */
+} B200kRowNormArgs;
+
+int b200k_rownorm(const B200kRowNormArgs* args, void* stream);
+
+/* Row softmax (or log-softmax) over the last dim, fp32 math, like aten._softmax. */
+typedef struct {
+  int64_t rows, cols;
+  const void* x;
+  int64_t x_row_stride;
+  int32_t x_dtype;
+  int32_t log_softmax;
+  void* out;
+  int64_t out_row_stride;
+  int32_t out_dtype;
+  int32_t pad;
+} B200kSoftmaxArgs;
+
+int b200k_softmax(const B200kSoftmaxArgs* args, void* stream);
+
+const char* b200k_status_string(int code);
+/* Library version, for the loader's sanity check. */
+int b200k_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200K_H */

@@ -1,0 +1,61 @@
+"""Backend switches and the kernel library's limits.
+
+Environment flags (read once at import, overridable as module attributes):
+  B200_EXTENSIONS=0   reference-identical grouping only: no view look-through
+                      for 3-d linears, no row-reduction fusion
+  B200_EPILOGUE=0     skip the GEMM+epilogue pass
+  B200_POINTWISE=0    skip the pointwise pass
+  B200_ROWREDUCE=0    skip the row-reduction pass
+  B200_DUMP=1         print each compiled graph and the fused-kernel programs
+
+The reference hard-codes its equivalents (AUTOTUNE_CONFIGS, BLOCK=1024,
+DOT_DTYPES in compiler/optimization/fusion_epilogue.py:23-38 and
+fusion_pointwise.py:229) and has no switches.
+"""
+from __future__ import annotations
+
+import os
+from typing import Callable
+
+import torch
+
+
+def _flag(name: str, default: bool) -> bool:
+    v = os.environ.get(name)
+    return default if v is None else v not in ("0", "false", "False", "")
+
+
+EXTENSIONS = _flag("B200_EXTENSIONS", True)
+ENABLE_EPILOGUE = _flag("B200_EPILOGUE", True)
+ENABLE_POINTWISE = _flag("B200_POINTWISE", True)
+ENABLE_ROWREDUCE = _flag("B200_ROWREDUCE", True)
+DUMP = _flag("B200_DUMP", False)
+
+# Kernel library limits (include/b200k.h).
+MAX_INPUTS = 8
+MAX_DIMS = 6
+LOADABLE_DTYPES = {
+    torch.float32, torch.float16, torch.bfloat16, torch.float64,
+    torch.int32, torch.int64, torch.bool, torch.uint8,
+}
+STORABLE_DTYPES = {torch.float32, torch.float16, torch.bfloat16, torch.float64}
+GEMM_AB_DTYPES = {torch.float16, torch.bfloat16}
+GEMM_OUT_DTYPES = {torch.float16, torch.bfloat16, torch.float32}
+ROW_DTYPES = {torch.float32, torch.float16, torch.bfloat16}
+
+# The fusions fire only for tensors on this predicate's device: CUDA, as in the
+# reference (fusion_pointwise.py:93, fusion_epilogue.py:41-42).  Tests that
+# inspect the rewritten graph on a CPU-only machine swap it out.
+_device_predicate: Callable[[torch.Tensor], bool] = lambda val: val.is_cuda
+
+
+def on_target_device(val: torch.Tensor) -> bool:
+    return _device_predicate(val)
+
+
+def set_device_predicate(fn: Callable[[torch.Tensor], bool]) -> Callable[[torch.Tensor], bool]:
+    """Replace the device predicate; returns the previous one."""
+    global _device_predicate
+    old = _device_predicate
+    _device_predicate = fn
+    return old

@@ -1,0 +1,271 @@
+"""Lowering of a fused FX group to the kernel library's epilogue program.
+
+The reference turns each group into Triton source, one SSA line per node
+(compiler/optimization/fusion_pointwise.py:139-152, emit_pointwise_ops), and
+JIT-compiles it.  Here a group becomes data instead: a short program for the
+accumulator machine that every pointwise and GEMM-epilogue kernel in
+libb200k.so interprets per element (include/b200k.h documents the
+instruction set).  No source is generated and nothing is compiled at run
+time.
+
+Machine model: one accumulator, ``MAX_SLOTS`` value slots.  Operands (the
+group's external inputs, or for a GEMM epilogue the accumulator and the extra
+tensors) arrive pre-loaded in slots 0..n-1.  Every binary op reads the
+accumulator and a slot or an immediate; values still needed later are spilled
+to a free slot before the accumulator is overwritten.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+import torch.fx as fx
+
+aten = torch.ops.aten
+
+# Mirror of the enums in include/b200k.h.
+MAX_SLOTS = 8
+MAX_INSTR = 64
+MAX_INPUTS = 8
+OPERAND_IMM = 8
+OPERAND_NONE = 9
+
+OP = {
+    "NOP": 0, "MOV": 1, "STORE": 2, "ADD": 3, "SUB": 4, "RSUB": 5, "MUL": 6, "DIV": 7, "RDIV": 8,
+    "MAX": 9, "MIN": 10, "NEG": 11, "ABS": 12, "RELU": 13, "EXP": 14, "LOG": 15, "SQRT": 16,
+    "RSQRT": 17, "ERF": 18, "SIGMOID": 19, "TANH": 20, "ROUND_BF16": 21, "ROUND_F16": 22,
+}
+OP_NAME = {v: k for k, v in OP.items()}
+
+# ATen op -> (machine op, swapped-operand machine op or None, is_unary).
+# The set is exactly the reference's POINTWISE_OPS
+# (compiler/optimization/fusion_pointwise.py:35-53); _to_copy is an identity
+# inside a kernel (the final store rounds to the output dtype).
+BINARY = {
+    aten.add.Tensor: ("ADD", "ADD"),
+    aten.sub.Tensor: ("SUB", "RSUB"),
+    aten.mul.Tensor: ("MUL", "MUL"),
+    aten.div.Tensor: ("DIV", "RDIV"),
+    aten.maximum.default: ("MAX", "MAX"),
+    aten.minimum.default: ("MIN", "MIN"),
+}
+UNARY = {
+    aten.neg.default: "NEG",
+    aten.abs.default: "ABS",
+    aten.relu.default: "RELU",
+    aten.exp.default: "EXP",
+    aten.log.default: "LOG",
+    aten.sqrt.default: "SQRT",
+    aten.rsqrt.default: "RSQRT",
+    aten.erf.default: "ERF",
+    aten.sigmoid.default: "SIGMOID",
+    aten.tanh.default: "TANH",
+}
+CAST = aten._to_copy.default
+
+
+class ProgramError(ValueError):
+    """The group does not fit the machine (too many live values or instructions)."""
+
+
+@dataclass
+class Program:
+    code: list[int] = field(default_factory=list)
+    imm: list[float] = field(default_factory=list)
+
+    def emit(self, op: str, operand: int = OPERAND_NONE, imm: float = 0.0) -> None:
+        if len(self.code) >= MAX_INSTR:
+            raise ProgramError(f"program longer than {MAX_INSTR} instructions")
+        self.code.append(OP[op] * 10 + operand)
+        self.imm.append(float(imm))
+
+    def __len__(self) -> int:
+        return len(self.code)
+
+    def listing(self) -> str:
+        out = []
+        for c, v in zip(self.code, self.imm):
+            op, operand = OP_NAME[c // 10], c % 10
+            arg = "" if operand == OPERAND_NONE else (f"#{v!r}" if operand == OPERAND_IMM else f"s{operand}")
+            out.append(f"{op} {arg}".strip())
+        return "; ".join(out)
+
+
+def round_op_for(dtype: torch.dtype) -> str | None:
+    if dtype == torch.bfloat16:
+        return "ROUND_BF16"
+    if dtype == torch.float16:
+        return "ROUND_F16"
+    return None
+
+
+def compile_group(
+    group: list[fx.Node],
+    operands: list[fx.Node],
+    prologue: list[tuple[str, fx.Node | float]] | None = None,
+    prologue_target: fx.Node | None = None,
+    rounding_casts: bool = False,
+) -> Program:
+    """Lower ``group`` (topologically ordered, last node = output) to a program.
+
+    ``operands[i]`` is pre-loaded in slot i.  ``prologue`` optionally rewrites
+    the value of ``prologue_target`` (an operand) before the group runs, e.g.
+    the addmm bias add ``acc = acc + bias`` (fusion_epilogue.py:142-143).
+    With ``rounding_casts`` a cast to bf16/f16 inside the group emits a
+    rounding op (used by fusions that cross sub-fp32 casts); otherwise casts
+    are identities as in the reference.
+    """
+    prog = Program()
+    members = set(group)
+
+    # Casts alias their input unless they round.
+    alias: dict[fx.Node, fx.Node] = {}
+
+    def canon(n):
+        while isinstance(n, fx.Node) and n in alias:
+            n = alias[n]
+        return n
+
+    rounding: dict[fx.Node, str] = {}
+    for node in group:
+        if node.target == CAST:
+            r = round_op_for(node.kwargs.get("dtype")) if rounding_casts and node is not group[-1] else None
+            if r is None:
+                alias[node] = node.args[0]
+            else:
+                rounding[node] = r
+
+    # Last use (index into group) of every canonical value read by the group.
+    last_use: dict[fx.Node, int] = {}
+    for i, node in enumerate(group):
+        if node in alias:
+            continue
+        for a in node.args:
+            if isinstance(a, fx.Node):
+                last_use[canon(a)] = i
+    root = canon(group[-1])
+    last_use[root] = len(group)  # the result is read by the final store
+
+    slot_of: dict[fx.Node, int] = {}
+    free = list(range(MAX_SLOTS))
+    for i, op in enumerate(operands):
+        if i >= MAX_SLOTS:
+            raise ProgramError("more operands than slots")
+        slot_of[op] = i
+        free.remove(i)
+    acc: fx.Node | None = None  # value currently in the accumulator
+
+    def release(i: int) -> None:
+        # Values whose last reader is node i (or that no node reads) give back their slot.
+        for v in list(slot_of):
+            if last_use.get(v, -1) <= i:
+                free.append(slot_of.pop(v))
+        free.sort()
+
+    def spill_acc() -> None:
+        nonlocal acc
+        if acc is not None and acc not in slot_of and last_use.get(acc, -1) >= cur_index:
+            if not free:
+                raise ProgramError(f"more than {MAX_SLOTS} live values")
+            s = free.pop(0)
+            prog.emit("STORE", s)
+            slot_of[acc] = s
+
+    def load_acc(v: fx.Node) -> None:
+        nonlocal acc
+        if acc is v:
+            return
+        spill_acc()
+        if v not in slot_of:
+            raise ProgramError(f"value {v} is neither in the accumulator nor in a slot")
+        prog.emit("MOV", slot_of[v])
+        acc = v
+
+    def operand_of(x) -> tuple[int, float]:
+        if isinstance(x, fx.Node):
+            v = canon(x)
+            if v is acc and v not in slot_of:
+                spill_acc()
+            if v not in slot_of:
+                raise ProgramError(f"value {v} not materialised")
+            return slot_of[v], 0.0
+        return OPERAND_IMM, float(x)
+
+    cur_index = -1
+    if prologue:
+        target = prologue_target
+        load_acc(target)
+        for op, x in prologue:
+            s, imm = operand_of(x)
+            prog.emit(op, s, imm)
+        # The operand's slot now holds a stale value: re-home the rewritten one.
+        prog.emit("STORE", slot_of[target])
+
+    for i, node in enumerate(group):
+        cur_index = i
+        if node in alias:
+            continue
+        if node in rounding:
+            src = canon(node.args[0])
+            load_acc(src)
+            # `src` stays needed after this node only if it is in a slot.
+            if last_use.get(src, -1) > i and src not in slot_of:
+                spill_acc()
+            prog.emit(rounding[node])
+            acc = node
+        elif node.target in UNARY:
+            src = canon(node.args[0])
+            if not isinstance(src, fx.Node):
+                raise ProgramError("unary op on a scalar")
+            load_acc(src)
+            if last_use.get(src, -1) > i and src not in slot_of:
+                spill_acc()
+            prog.emit(UNARY[node.target])
+            acc = node
+        elif node.target in BINARY:
+            op, swapped = BINARY[node.target]
+            a, b = (canon(x) if isinstance(x, fx.Node) else x for x in node.args[:2])
+            if isinstance(a, fx.Node) and acc is a:
+                left, right, mop = a, b, op
+            elif isinstance(b, fx.Node) and acc is b:
+                left, right, mop = b, a, swapped
+            elif isinstance(a, fx.Node):
+                left, right, mop = a, b, op
+            elif isinstance(b, fx.Node):
+                left, right, mop = b, a, swapped
+            else:
+                raise ProgramError("binary op on two scalars")
+            load_acc(left)
+            # Keep `left` if a later node (or this node's right operand) reads it.
+            if (last_use.get(left, -1) > i or right is left) and left not in slot_of:
+                spill_acc()
+            s, imm = operand_of(right)
+            prog.emit(mop, s, imm)
+            acc = node
+        else:
+            raise ProgramError(f"unsupported op {node.target}")
+        release(i)
+
+    if acc is not root:
+        load_acc(root)
+    return prog
+
+
+def group_spec(group: list[fx.Node], operands: list[fx.Node]) -> list[tuple]:
+    """A plain-data description of a group (op name, args as ('in', i) /
+    ('node', j) / float), used to evaluate the same group in the oracle."""
+    index = {n: j for j, n in enumerate(group)}
+    opi = {n: i for i, n in enumerate(operands)}
+    spec = []
+    for node in group:
+        args = []
+        for a in node.args:
+            if isinstance(a, fx.Node):
+                args.append(("node", index[a]) if a in index else ("in", opi[a]))
+            else:
+                args.append(float(a))
+        name = str(node.target).replace("aten.", "")
+        if node.target == CAST:
+            args.append(str(node.kwargs.get("dtype")).replace("torch.", ""))
+        spec.append((name, tuple(args)))
+    return spec

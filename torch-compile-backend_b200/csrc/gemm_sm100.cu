@@ -1,0 +1,730 @@
+// GEMM + fused epilogue on the sm_100a tensor cores.
+//
+//   out[m, n] = program(acc[m, n], extras...[m, n]),  acc = sum_k a[m, k] * b[k, n]
+//
+// Replaces the reference's generated, autotuned Triton kernel
+// (compiler/optimization/fusion_epilogue.py:72-151, launched by :164-177, tile
+// candidates :31-38) and the standalone demos hand_written/gemm_kernel.py and
+// hand_written/gemm_swizzled_kernel.py.
+//
+// Design (one CTA per SM, persistent, warp-specialised, 384 threads):
+//   warp 0      TMA producer: one thread streams 128xBK tiles of A and BNxBK
+//               tiles of B into a STAGES-deep shared-memory ring (128-byte
+//               swizzle), completing `full[s]` mbarriers by transaction count.
+//   warp 1      MMA issuer: one thread issues tcgen05.mma (kind::f16, fp32
+//               accumulate, M=128, N=BN, K=16) from smem descriptors into one
+//               of two TMEM accumulators, releases ring slots with
+//               tcgen05.commit -> empty[s], and hands a finished accumulator to
+//               the epilogue with tcgen05.commit -> tmem_full[acc].
+//   warp 2      owns the TMEM allocation (2*BN columns).
+//   warps 4..11 epilogue, two warps per SM sub-partition: warp w reads TMEM
+//               lane quarter (w % 4) and one half of the tile's columns with
+//               tcgen05.ld (one output row per thread), runs the epilogue
+//               program in registers (bias, activation, residual, scale,
+//               casts) while the next 8 columns' operands are in flight, packs
+//               to the output dtype into a swizzled smem tile and stores it
+//               with a TMA bulk-tensor store.  It frees the accumulator with
+//               tmem_empty[acc] so the MMA warp can start tile i+2 while tile
+//               i+1 accumulates into the other buffer.
+// Tiles are visited in grouped order (GROUP_M tiles down M per column band)
+// so that co-resident CTAs share A and B panels in L2.
+//
+// Every mbarrier wait is bounded (global timer): on timeout the kernel records
+// B200K_ERR_TIMEOUT in the caller's status word, raises a CTA abort flag so the
+// other roles leave their loops, drains what it has in flight, frees TMEM and
+// returns.
+#include <cuda.h>
+
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "common.cuh"
+#include "host_common.h"
+
+namespace b200k {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // one 128-byte swizzle atom of 16-bit elements
+constexpr int UMMA_K = 16;
+constexpr int kEpiWarps = 8;               // two per SM sub-partition
+constexpr int kThreads = 128 + 32 * kEpiWarps;  // warps 0-3 control, 4.. epilogue
+constexpr int kGroupM = 16;
+constexpr uint32_t kStgBytes = 32 * 128;  // one epilogue warp's 32 rows x 128 bytes
+
+struct EpiOperand {
+  const void* ptr;
+  int64_t sm, sn;
+  int32_t dt;
+  int32_t vec;  // 8-wide loads along n are legal
+};
+
+struct Params {
+  int32_t M, N, K;
+  int32_t tiles_m, tiles_n, num_tiles, k_blocks;
+  int32_t n_extras;
+  int32_t out_dt;
+  int32_t direct_store;  // 1: write with st.global (output not TMA-storable)
+  void* out;
+  int64_t out_sm;
+  int32_t* status;
+  int64_t timeout_ns;
+  uint32_t idesc;
+  int32_t pad;
+  EpiOperand ex[B200K_MAX_INPUTS - 1];
+  B200kProgram prog;
+};
+
+// ----------------------------------------------------------------- PTX wrappers
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(map),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* m) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(m) : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor (tcgen05 format): start address, leading and
+// stride byte offsets (16-byte units), descriptor version 1, 128-byte swizzle.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16;
+  d |= static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32;
+  d |= static_cast<uint64_t>(1) << 46;
+  d |= static_cast<uint64_t>(2) << 61;
+  return d;
+}
+
+// ------------------------------------------------------------- bounded waits
+struct Ctl {
+  volatile int* abort;
+  int32_t* status;
+  uint64_t timeout_ns;
+};
+
+// Waits for the phase of `bar` with parity `parity`.  Returns false when the
+// CTA is aborting or this wait ran out of time (then it raises the abort).
+__device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Ctl& c) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 0) {
+      if (*c.abort) return false;
+      if (global_timer_ns() - t0 > c.timeout_ns) {
+        *c.abort = 1;
+        if (c.status) atomicCAS(c.status, 0, B200K_ERR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+// Same, ignoring the abort flag: used only to drain in-flight async work.
+__device__ __forceinline__ bool wait_bar_drain(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (global_timer_ns() - t0 > limit_ns) return false;
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {
+  const int per_group = kGroupM * p.tiles_n;
+  const int g = t / per_group;
+  const int first_m = g * kGroupM;
+  const int gsize = min(p.tiles_m - first_m, kGroupM);
+  const int r = t - g * per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+// Epilogue operand values at (m, n..n+3), zero outside [M, N).
+__device__ __forceinline__ void load_extra4(const EpiOperand& e, int m, int n, int M, int N, float (&v)[4]) {
+  if (m < M && n + 4 <= N && e.vec) {
+    const int64_t off = static_cast<int64_t>(m) * e.sm + n;
+    if (e.dt == B200K_F32) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(reinterpret_cast<const float*>(e.ptr) + off));
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+      const uint2 u = __ldg(reinterpret_cast<const uint2*>(reinterpret_cast<const uint16_t*>(e.ptr) + off));
+      if (e.dt == B200K_BF16) {
+        const float2 lo = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+        const float2 hi = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+        v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+      } else {
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+      }
+    }
+  } else if (e.sn == 0) {
+    const float s = (m < M) ? load_scalar(e.ptr, static_cast<int64_t>(m) * e.sm, e.dt) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[j] = s;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v[j] = (m < M && n + j < N)
+                 ? load_scalar(e.ptr, static_cast<int64_t>(m) * e.sm + static_cast<int64_t>(n + j) * e.sn, e.dt)
+                 : 0.0f;
+  }
+}
+
+// 32 lanes x 32 bit, 4 consecutive columns.
+__device__ __forceinline__ void tmem_ld4(uint32_t taddr, uint32_t (&r)[4]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(taddr));
+}
+
+constexpr int kEV = 4;  // epilogue group width (columns per interpreter pass)
+using ExtraRegs = float[B200K_MAX_INPUTS - 1][kEV];
+
+__device__ __forceinline__ void load_extras(const Params& p, int m, int n, ExtraRegs& x) {
+#pragma unroll
+  for (int i = 0; i < B200K_MAX_INPUTS - 1; ++i)
+    if (i < p.n_extras) load_extra4(p.ex[i], m, n, p.M, p.N, x[i]);
+}
+
+// One 4-column group of one output row: TMEM -> registers, issue the next
+// group's operand loads (`nxt`), run the program, pack into the swizzled
+// staging row (or store directly when the output is not TMA-storable).
+template <int OUT_BYTES>
+__device__ __forceinline__ void epilogue_group(const Params& p, uint32_t taddr, int m, int n, int g, int lane,
+                                               uint8_t* sb, const ExtraRegs& cur, ExtraRegs& nxt, bool prefetch) {
+  uint32_t raw[kEV];
+  tmem_ld4(taddr, raw);
+  if (prefetch) load_extras(p, m, n + kEV, nxt);
+  tmem_wait_ld();
+  float r[kSlots][kEV];
+  float accv[kEV];
+#pragma unroll
+  for (int j = 0; j < kEV; ++j) {
+    r[0][j] = __uint_as_float(raw[j]);
+    accv[j] = r[0][j];
+  }
+#pragma unroll
+  for (int i = 0; i < B200K_MAX_INPUTS - 1; ++i)
+    if (i < p.n_extras) {
+#pragma unroll
+      for (int j = 0; j < kEV; ++j) r[i + 1][j] = cur[i][j];
+    }
+  run_program<kEV>(p.prog, r, accv);
+  if (p.direct_store) {
+    if (m < p.M) {
+      const int64_t off = static_cast<int64_t>(m) * p.out_sm + n;
+#pragma unroll
+      for (int j = 0; j < kEV; ++j)
+        if (n + j < p.N) store_scalar(p.out, off + j, p.out_dt, accv[j]);
+    }
+  } else if (OUT_BYTES == 2) {
+    uint2 u;
+    if (p.out_dt == B200K_BF16) {
+      *reinterpret_cast<__nv_bfloat162*>(&u.x) = __floats2bfloat162_rn(accv[0], accv[1]);
+      *reinterpret_cast<__nv_bfloat162*>(&u.y) = __floats2bfloat162_rn(accv[2], accv[3]);
+    } else {
+      *reinterpret_cast<__half2*>(&u.x) = __floats2half2_rn(accv[0], accv[1]);
+      *reinterpret_cast<__half2*>(&u.y) = __floats2half2_rn(accv[2], accv[3]);
+    }
+    const int chunk = g >> 1;
+    *reinterpret_cast<uint2*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4) + ((g & 1) << 3)) = u;
+  } else {
+    *reinterpret_cast<float4*>(sb + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+        make_float4(accv[0], accv[1], accv[2], accv[3]);
+  }
+}
+
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
+struct Cfg {
+  static constexpr uint32_t kABytes = BM * BK * 2;
+  static constexpr uint32_t kBBytes = BN * BK * 2;
+  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr int kEC = 128 / OUT_BYTES;  // output columns per 128-byte staging row
+  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + kEpiWarps * kStgBytes;
+  static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
+};
+
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
+  using C = Cfg<BN, STAGES, B_NMAJOR, OUT_BYTES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sbase = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sA = sbase;
+  uint8_t* sB = sA + STAGES * C::kABytes;
+  uint8_t* sStg = sB + STAGES * C::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + C::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], kEpiWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&tmA);
+    prefetch_map(&tmB);
+    if (!p.direct_store) prefetch_map(&tmO);
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const Ctl ctl{abort_flag, p.status, static_cast<uint64_t>(p.timeout_ns)};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        int tm, tn;
+        tile_coords(t, p, tm, tn);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&empty[s], ph ^ 1u, ctl)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
+          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * BK, tm * BM);
+          if (B_NMAJOR) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sB + s * C::kBBytes + j * (64 * BK * 2), &tmB, &full[s], tn * BN + j * 64, kb * BK);
+          } else {
+            tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * BK, tn * BN);
+          }
+          ++issued;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        // Let every load still in flight land before the CTA can exit.
+        for (int x = 0; x < STAGES; ++x) {
+          if (issued > x) {
+            const uint32_t par = (x < s) ? ph : (ph ^ 1u);
+            wait_bar_drain(&full[x], par, 100000000ull);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < p.num_tiles && ok; t += gridDim.x) {
+        if (!wait_bar(&tempty[acc], aph ^ 1u, ctl)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&full[s], ph, ctl)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * C::kABytes);
+          const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k) {
+            const uint64_t ad = sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024);
+            const uint64_t bd = B_NMAJOR ? sw128_desc(b0 + k * (UMMA_K * 128), 64 * BK * 2, 1024)
+                                         : sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024);
+            umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[s]);
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1u;
+        }
+      }
+      // Every MMA this thread issued completes before TMEM can be released.
+      umma_commit(drain);
+      wait_bar_drain(drain, 0, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    // Warp w reads TMEM lane quarter (w % 4) and one half of the tile's columns.
+    const int ew = warp - 4;
+    const int quarter = warp & 3;
+    const int half = ew >> 2;
+    uint8_t* sb = sStg + ew * kStgBytes;
+    int acc = 0;
+    uint32_t aph = 0;
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+      int tm, tn;
+      tile_coords(t, p, tm, tn);
+      if (!wait_bar(&tfull[acc], aph, ctl)) break;
+      tc_fence_after();
+      const int m = tm * BM + quarter * 32 + lane;
+      const int ncol0 = tn * BN + half * (BN / 2);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + half * (BN / 2));
+#pragma unroll 1
+      for (int c = 0; c < (BN / 2) / C::kEC; ++c) {
+        const int n0 = ncol0 + c * C::kEC;
+        if (n0 >= p.N) break;
+        if (!p.direct_store) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
+        ExtraRegs xa, xb;
+        load_extras(p, m, n0, xa);
+#pragma unroll 1
+        for (int g = 0; g < C::kEC / kEV; g += 2) {
+          epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + g * kEV, m, n0 + g * kEV, g, lane, sb, xa, xb, true);
+          epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + (g + 1) * kEV, m, n0 + (g + 1) * kEV, g + 1, lane, sb, xb,
+                                    xa, g + 2 < C::kEC / kEV);
+        }
+        if (!p.direct_store) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmO, sb, n0, tm * BM + quarter * 32);
+            bulk_commit();
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        aph ^= 1u;
+      }
+    }
+    if (!p.direct_store && lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ----------------------------------------------------------------- host side
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(f);
+  });
+  return fn;
+}
+
+CUtensorMapDataType tma_dtype(int dt) {
+  switch (dt) {
+    case B200K_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case B200K_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    default: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  }
+}
+
+// 2-d tiled map over a row-major view: `inner` elements contiguous, `outer`
+// rows `row_bytes` apart; box = box_inner x box_outer; 128-byte swizzle.
+bool make_map(CUtensorMap* map, int dt, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+              uint32_t box_inner, uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {row_bytes};
+  const cuuint32_t box[2] = {box_inner, box_outer};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, tma_dtype(dt), 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+struct TileConfig {
+  int bn, stages;
+};
+constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}};
+constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
+
+template <int BN, int STAGES, bool BNM, int OB>
+int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
+               cudaStream_t st) {
+  using C = Cfg<BN, STAGES, BNM, OB>;
+  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB>;
+  static bool attr_set = false;  // per instantiation; idempotent
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+      return B200K_ERR_LAUNCH;
+    attr_set = true;
+  }
+  kern<<<grid, kThreads, C::kSmem, st>>>(ta, tb, to, p);
+  return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
+}
+
+template <int BN, int STAGES>
+int launch_cfg(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+               const Params& p, int grid, cudaStream_t st) {
+  if (bnm) {
+    return ob == 2 ? launch_one<BN, STAGES, true, 2>(ta, tb, to, p, grid, st)
+                   : launch_one<BN, STAGES, true, 4>(ta, tb, to, p, grid, st);
+  }
+  return ob == 2 ? launch_one<BN, STAGES, false, 2>(ta, tb, to, p, grid, st)
+                 : launch_one<BN, STAGES, false, 4>(ta, tb, to, p, grid, st);
+}
+
+int pick(int64_t M, int64_t N, int sms) {
+  // Per-SM time of a config ~ (tiles per SM, rounded up) x (tile width); the
+  // narrower tile pays ~10% more for the same work (it re-reads A twice as
+  // often and runs the MMA at N=128).
+  int best = 0;
+  double best_cost = 1e300;
+  for (int c = 0; c < kNumConfigs; ++c) {
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + kConfigs[c].bn - 1) / kConfigs[c].bn);
+    const int64_t per_sm = (tiles + sms - 1) / sms;
+    const double cost = static_cast<double>(per_sm) * kConfigs[c].bn * (kConfigs[c].bn == 256 ? 1.0 : 1.1);
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = c;
+    }
+  }
+  return best;
+}
+
+}  // namespace gemm
+
+int device_sm_count() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  return sms;
+}
+
+}  // namespace b200k
+
+using namespace b200k;
+using namespace b200k::gemm;
+
+extern "C" int b200k_gemm_num_configs(void) { return kNumConfigs; }
+
+extern "C" int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages) {
+  if (config < 0 || config >= kNumConfigs) return B200K_ERR_ARG;
+  if (block_m) *block_m = BM;
+  if (block_n) *block_n = kConfigs[config].bn;
+  if (block_k) *block_k = BK;
+  if (stages) *stages = kConfigs[config].stages;
+  return B200K_OK;
+}
+
+extern "C" int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K) {
+  (void)K;
+  int sms = device_sm_count();
+  if (sms <= 0) sms = 148;
+  return pick(M, N, sms);
+}
+
+extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
+  if (!a || !a->a || !a->b || !a->out) return B200K_ERR_ARG;
+  if (a->M < 0 || a->N < 0 || a->K < 0) return B200K_ERR_SHAPE;
+  if (a->M == 0 || a->N == 0) return B200K_OK;
+  if (a->K == 0) return B200K_ERR_SHAPE;
+  if (a->M > 0x7fffffff || a->N > 0x7fffffff || a->K > 0x7fffffff) return B200K_ERR_SHAPE;
+  if (a->ab_dtype != B200K_BF16 && a->ab_dtype != B200K_F16) return B200K_ERR_UNSUPPORTED;
+  if (a->out_dtype != B200K_BF16 && a->out_dtype != B200K_F16 && a->out_dtype != B200K_F32)
+    return B200K_ERR_UNSUPPORTED;
+  if (a->n_extras < 0 || a->n_extras > B200K_MAX_INPUTS - 1) return B200K_ERR_ARG;
+  int rc = validate_program(a->program, 1 + a->n_extras);
+  if (rc != B200K_OK) return rc;
+
+  // A: [M, K], unit K stride, rows 16-byte aligned.
+  if (a->a_stride_k != 1 && a->K > 1) return B200K_ERR_UNSUPPORTED;
+  if (!aligned16(a->a) || (a->a_stride_m * 2) % 16 != 0) return B200K_ERR_ALIGN;
+  // B: K-major (unit K stride) or N-major (unit N stride).
+  bool bnm;
+  if (a->b_stride_k == 1) {
+    bnm = false;
+    if (!aligned16(a->b) || (a->b_stride_n * 2) % 16 != 0) return B200K_ERR_ALIGN;
+  } else if (a->b_stride_n == 1) {
+    bnm = true;
+    if (!aligned16(a->b) || (a->b_stride_k * 2) % 16 != 0) return B200K_ERR_ALIGN;
+  } else {
+    return B200K_ERR_UNSUPPORTED;
+  }
+  if (a->out_stride_n != 1 && a->N > 1) return B200K_ERR_UNSUPPORTED;
+  for (int i = 0; i < a->n_extras; ++i) {
+    if (!a->extras[i].ptr) return B200K_ERR_ARG;
+    if (!valid_dtype(a->extras[i].dtype)) return B200K_ERR_UNSUPPORTED;
+  }
+
+  const int sms = device_sm_count();
+  if (sms <= 0) return B200K_ERR_DEVICE;
+  int cfg = a->tile_config;
+  if (cfg < 0) cfg = pick(a->M, a->N, sms);
+  if (cfg >= kNumConfigs) return B200K_ERR_ARG;
+  const int bn = kConfigs[cfg].bn;
+  const int ob = a->out_dtype == B200K_F32 ? 4 : 2;
+
+  Params p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = static_cast<int32_t>(a->M);
+  p.N = static_cast<int32_t>(a->N);
+  p.K = static_cast<int32_t>(a->K);
+  p.tiles_m = static_cast<int32_t>((a->M + BM - 1) / BM);
+  p.tiles_n = static_cast<int32_t>((a->N + bn - 1) / bn);
+  const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
+  if (tiles > 0x7fffffff) return B200K_ERR_SHAPE;
+  p.num_tiles = static_cast<int32_t>(tiles);
+  p.k_blocks = static_cast<int32_t>((a->K + BK - 1) / BK);
+  p.n_extras = a->n_extras;
+  p.out_dt = a->out_dtype;
+  p.out = a->out;
+  p.out_sm = a->out_stride_m;
+  p.status = a->status;
+  p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 2000000000ll;
+  const uint32_t fmt = a->ab_dtype == B200K_BF16 ? 1u : 0u;
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
+            (static_cast<uint32_t>(BM >> 4) << 24);
+  for (int i = 0; i < a->n_extras; ++i) {
+    const B200kEpiOperand& e = a->extras[i];
+    EpiOperand& q = p.ex[i];
+    q.ptr = e.ptr;
+    q.sm = e.stride_m;
+    q.sn = e.stride_n;
+    q.dt = e.dtype;
+    const int dt = e.dtype;
+    q.vec = (e.stride_n == 1 && aligned16(e.ptr) && e.stride_m % 8 == 0 &&
+             (dt == B200K_BF16 || dt == B200K_F16 || dt == B200K_F32))
+                ? 1
+                : 0;
+  }
+  p.prog = a->program;
+
+  CUtensorMap ta, tb, to;
+  std::memset(&to, 0, sizeof(to));
+  if (!make_map(&ta, a->ab_dtype, a->a, a->K, a->M, a->a_stride_m * 2, BK, BM)) return B200K_ERR_LAUNCH;
+  if (bnm) {
+    if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * 2, 64, BK)) return B200K_ERR_LAUNCH;
+  } else {
+    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, bn)) return B200K_ERR_LAUNCH;
+  }
+  const bool tma_out = aligned16(a->out) && (a->out_stride_m * ob) % 16 == 0;
+  p.direct_store = tma_out ? 0 : 1;
+  if (tma_out) {
+    if (!make_map(&to, a->out_dtype, a->out, a->N, a->M, a->out_stride_m * ob, 128 / ob, 32)) return B200K_ERR_LAUNCH;
+  }
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (cfg == 0) return launch_cfg<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
+  return launch_cfg<128, 6>(bnm, ob, ta, tb, to, p, grid, st);
+}

@@ -1,0 +1,341 @@
+// Thin PyTorch binding: registers torch.ops.b200.* (CUDA dispatch key) and
+// forwards each call to the C ABI of libb200k.so (include/b200k.h).
+//
+// These ops are what the rewritten FX graph calls in place of the reference's
+// Python closures `fused_op(*tensors)` (compiler/optimization/
+// fusion_pointwise.py:224-230) and `epilogue_op(a, b, *tensors)`
+// (compiler/optimization/fusion_epilogue.py:164-177).  Like those closures they
+// allocate the output with the caching allocator (torch.empty) and launch on
+// the current stream; unlike them they never fall back to anything: a
+// library error becomes a RuntimeError.
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/library.h>
+
+#include <mutex>
+#include <vector>
+
+#include "b200k.h"
+
+namespace {
+
+int to_dt(at::ScalarType t) {
+  switch (t) {
+    case at::kFloat: return B200K_F32;
+    case at::kHalf: return B200K_F16;
+    case at::kBFloat16: return B200K_BF16;
+    case at::kDouble: return B200K_F64;
+    case at::kInt: return B200K_I32;
+    case at::kLong: return B200K_I64;
+    case at::kBool: return B200K_BOOL;
+    case at::kByte: return B200K_U8;
+    default: TORCH_CHECK(false, "b200: unsupported dtype ", t);
+  }
+  return -1;
+}
+
+void check(int rc, const char* what) {
+  TORCH_CHECK(rc == B200K_OK, "b200::", what, " failed: ", b200k_status_string(rc), " (code ", rc, ")");
+}
+
+B200kProgram make_program(at::IntArrayRef code, at::ArrayRef<double> imm) {
+  TORCH_CHECK(code.size() == imm.size(), "b200: program code/imm length mismatch");
+  TORCH_CHECK(static_cast<int64_t>(code.size()) <= B200K_MAX_INSTR, "b200: program too long (", code.size(), ")");
+  B200kProgram p;
+  std::memset(&p, 0, sizeof(p));
+  p.n = static_cast<int32_t>(code.size());
+  for (size_t i = 0; i < code.size(); ++i) {
+    p.ins[i].code = static_cast<int32_t>(code[i]);
+    p.ins[i].imm = static_cast<float>(imm[i]);
+  }
+  return p;
+}
+
+void* stream_of(const at::Tensor& t) {
+  return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
+}
+
+// Per-device status word the GEMM kernel writes when a wait times out.
+at::Tensor& status_word(int dev) {
+  static std::mutex mu;
+  static std::vector<at::Tensor> words;
+  std::lock_guard<std::mutex> lock(mu);
+  if (static_cast<int>(words.size()) <= dev) words.resize(dev + 1);
+  if (!words[dev].defined())
+    words[dev] = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(at::kCUDA, dev));
+  return words[dev];
+}
+
+at::Tensor pointwise(at::TensorList inputs, at::IntArrayRef code, at::ArrayRef<double> imm,
+                     at::IntArrayRef out_shape, at::ScalarType out_dtype) {
+  TORCH_CHECK(!inputs.empty() && inputs.size() <= B200K_MAX_INPUTS, "b200::pointwise: 1..8 inputs, got ",
+              inputs.size());
+  TORCH_CHECK(static_cast<int64_t>(out_shape.size()) <= B200K_MAX_DIMS, "b200::pointwise: rank > 6");
+  const at::Tensor& first = inputs[0];
+  TORCH_CHECK(first.is_cuda(), "b200::pointwise: inputs must be CUDA tensors");
+  c10::cuda::CUDAGuard guard(first.device());
+  at::Tensor out = at::empty(out_shape, first.options().dtype(out_dtype));
+  B200kPointwiseArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rank = static_cast<int32_t>(out_shape.size());
+  a.n_inputs = static_cast<int32_t>(inputs.size());
+  for (int d = 0; d < a.rank; ++d) a.sizes[d] = out_shape[d];
+  for (size_t i = 0; i < inputs.size(); ++i) {
+    const at::Tensor& t = inputs[i];
+    TORCH_CHECK(t.is_cuda() && t.device() == first.device(), "b200::pointwise: inputs on different devices");
+    const at::Tensor e = t.expand(out_shape);
+    a.inputs[i].ptr = e.data_ptr();
+    a.inputs[i].dtype = to_dt(e.scalar_type());
+    for (int d = 0; d < a.rank; ++d) a.inputs[i].strides[d] = e.stride(d);
+  }
+  a.out = out.data_ptr();
+  a.out_dtype = to_dt(out_dtype);
+  a.program = make_program(code, imm);
+  check(b200k_pointwise(&a, stream_of(first)), "pointwise");
+  return out;
+}
+
+// (m, n) strides of an epilogue operand broadcast to out_shape, whose leading
+// dims flatten into m.
+void mn_strides(const at::Tensor& t, at::IntArrayRef out_shape, int64_t& sm, int64_t& sn) {
+  const at::Tensor e = t.expand(out_shape);
+  const int r = static_cast<int>(out_shape.size());
+  TORCH_CHECK(r >= 1, "b200::gemm_epilogue: output rank 0");
+  sn = e.stride(r - 1);
+  if (r == 1) {
+    sm = 0;
+    return;
+  }
+  sm = e.stride(r - 2);
+  // Leading dims must merge into one index m with stride sm.
+  int64_t expect = sm * out_shape[r - 2];
+  for (int d = r - 3; d >= 0; --d) {
+    if (out_shape[d] != 1) {
+      TORCH_CHECK(e.stride(d) == expect, "b200::gemm_epilogue: epilogue operand leading dims do not flatten");
+    }
+    expect *= out_shape[d];
+  }
+}
+
+at::Tensor gemm_epilogue(const at::Tensor& a, const at::Tensor& b, at::TensorList extras, at::IntArrayRef code,
+                         at::ArrayRef<double> imm, at::IntArrayRef out_shape, at::ScalarType out_dtype) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "b200::gemm_epilogue: a and b must be CUDA tensors");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "b200::gemm_epilogue: a [M,K] and b [K,N] must be 2-d");
+  TORCH_CHECK(a.size(1) == b.size(0), "b200::gemm_epilogue: incompatible shapes ", a.sizes(), " and ", b.sizes());
+  TORCH_CHECK(a.scalar_type() == b.scalar_type(), "b200::gemm_epilogue: a and b dtypes differ");
+  TORCH_CHECK(static_cast<int64_t>(extras.size()) <= B200K_MAX_INPUTS - 1, "b200::gemm_epilogue: too many extras");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(1);
+  int64_t numel = 1;
+  for (auto s : out_shape) numel *= s;
+  TORCH_CHECK(numel == M * N && !out_shape.empty() && out_shape.back() == N,
+              "b200::gemm_epilogue: out_shape ", out_shape, " does not hold [", M, ", ", N, "]");
+  c10::cuda::CUDAGuard guard(a.device());
+  at::Tensor out = at::empty(out_shape, a.options().dtype(out_dtype));
+  B200kGemmArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.a = a.data_ptr();
+  g.a_stride_m = a.stride(0);
+  g.a_stride_k = a.stride(1);
+  g.b = b.data_ptr();
+  g.b_stride_k = b.stride(0);
+  g.b_stride_n = b.stride(1);
+  g.ab_dtype = to_dt(a.scalar_type());
+  g.out_dtype = to_dt(out_dtype);
+  g.out = out.data_ptr();
+  g.out_stride_m = N;
+  g.out_stride_n = 1;
+  g.n_extras = static_cast<int32_t>(extras.size());
+  g.tile_config = -1;
+  for (size_t i = 0; i < extras.size(); ++i) {
+    const at::Tensor& t = extras[i];
+    TORCH_CHECK(t.is_cuda() && t.device() == a.device(), "b200::gemm_epilogue: extras must be on a's device");
+    int64_t sm, sn;
+    mn_strides(t, out_shape, sm, sn);
+    g.extras[i].ptr = t.data_ptr();
+    g.extras[i].dtype = to_dt(t.scalar_type());
+    g.extras[i].stride_m = sm;
+    g.extras[i].stride_n = sn;
+  }
+  g.program = make_program(code, imm);
+  g.status = status_word(a.device().index()).data_ptr<int32_t>();
+  check(b200k_gemm_epilogue(&g, stream_of(a)), "gemm_epilogue");
+  return out;
+}
+
+int64_t gemm_status(int64_t device, bool reset) {
+  at::Tensor& w = status_word(static_cast<int>(device));
+  const int64_t v = w.item<int32_t>();
+  if (reset) w.zero_();
+  return v;
+}
+
+void rows_of(const at::Tensor& x, int64_t& rows, int64_t& cols, int64_t& row_stride) {
+  TORCH_CHECK(x.dim() >= 1, "b200: row op on a 0-d tensor");
+  cols = x.size(-1);
+  rows = cols == 0 ? 0 : x.numel() / cols;
+  TORCH_CHECK(x.stride(-1) == 1 || cols == 1, "b200: row op needs a unit last-dim stride");
+  row_stride = x.dim() >= 2 ? x.stride(-2) : cols;
+  int64_t expect = row_stride * (x.dim() >= 2 ? x.size(-2) : 1);
+  for (int d = static_cast<int>(x.dim()) - 3; d >= 0; --d) {
+    if (x.size(d) != 1) TORCH_CHECK(x.stride(d) == expect, "b200: row op needs leading dims that flatten");
+    expect *= x.size(d);
+  }
+  if (x.dim() < 2) row_stride = cols;
+}
+
+at::Tensor rms_norm_impl(const at::Tensor& x_in, const c10::optional<at::Tensor>& weight, double eps, int64_t flags,
+                         at::ScalarType out_dtype, bool swiglu) {
+  TORCH_CHECK(x_in.is_cuda(), "b200::rms_norm: x must be a CUDA tensor");
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const at::Tensor x = x_in.stride(-1) == 1 ? x_in : x_in.contiguous();
+  int64_t rows, cols, rs;
+  rows_of(x, rows, cols, rs);
+  std::vector<int64_t> oshape(x.sizes().begin(), x.sizes().end());
+  if (swiglu) {
+    TORCH_CHECK(cols % 2 == 0, "b200::rms_norm_swiglu: odd last dim");
+    oshape.back() = cols / 2;
+  }
+  at::Tensor out = at::empty(oshape, x.options().dtype(out_dtype));
+  B200kRowNormArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rows = rows;
+  a.cols = cols;
+  a.x = x.data_ptr();
+  a.x_row_stride = rs;
+  a.x_dtype = to_dt(x.scalar_type());
+  a.kind = swiglu ? B200K_ROW_RMSNORM_SWIGLU : B200K_ROW_RMSNORM;
+  at::Tensor w;
+  if (weight.has_value() && weight->defined()) {
+    w = weight->contiguous();
+    TORCH_CHECK(w.numel() == cols, "b200::rms_norm: weight has ", w.numel(), " elements, expected ", cols);
+    a.weight = w.data_ptr();
+    a.w_dtype = to_dt(w.scalar_type());
+  }
+  a.flags = static_cast<int32_t>(flags);
+  a.eps = static_cast<float>(eps);
+  a.out = out.data_ptr();
+  a.out_row_stride = oshape.back();
+  a.out_dtype = to_dt(out_dtype);
+  check(b200k_rownorm(&a, stream_of(x)), swiglu ? "rms_norm_swiglu" : "rms_norm");
+  return out;
+}
+
+at::Tensor rms_norm(const at::Tensor& x, const c10::optional<at::Tensor>& weight, double eps, int64_t flags,
+                    at::ScalarType out_dtype) {
+  return rms_norm_impl(x, weight, eps, flags, out_dtype, false);
+}
+at::Tensor rms_norm_swiglu(const at::Tensor& x, const c10::optional<at::Tensor>& weight, double eps, int64_t flags,
+                           at::ScalarType out_dtype) {
+  return rms_norm_impl(x, weight, eps, flags, out_dtype, true);
+}
+
+std::tuple<at::Tensor, at::Tensor, at::Tensor> layer_norm(const at::Tensor& x_in, at::IntArrayRef normalized_shape,
+                                                          const c10::optional<at::Tensor>& weight,
+                                                          const c10::optional<at::Tensor>& bias, double eps) {
+  TORCH_CHECK(x_in.is_cuda(), "b200::layer_norm: x must be a CUDA tensor");
+  TORCH_CHECK(normalized_shape.size() == 1, "b200::layer_norm: only last-dim normalisation is supported");
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const at::Tensor x = x_in.contiguous();
+  int64_t rows, cols, rs;
+  rows_of(x, rows, cols, rs);
+  TORCH_CHECK(cols == normalized_shape[0], "b200::layer_norm: normalized_shape mismatch");
+  at::Tensor out = at::empty(x.sizes(), x.options());
+  std::vector<int64_t> stat_shape(x.sizes().begin(), x.sizes().end());
+  stat_shape.back() = 1;
+  // native_layer_norm on CUDA keeps mean/rstd in fp32 for reduced-precision input.
+  const auto stat_dt = (x.scalar_type() == at::kDouble) ? at::kDouble : at::kFloat;
+  TORCH_CHECK(stat_dt == at::kFloat, "b200::layer_norm: fp64 input unsupported");
+  at::Tensor mean = at::empty(stat_shape, x.options().dtype(stat_dt));
+  at::Tensor rstd = at::empty(stat_shape, x.options().dtype(stat_dt));
+  B200kRowNormArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rows = rows;
+  a.cols = cols;
+  a.x = x.data_ptr();
+  a.x_row_stride = rs;
+  a.x_dtype = to_dt(x.scalar_type());
+  a.kind = B200K_ROW_LAYERNORM;
+  at::Tensor w, b;
+  if (weight.has_value() && weight->defined()) {
+    w = weight->contiguous();
+    a.weight = w.data_ptr();
+    a.w_dtype = to_dt(w.scalar_type());
+  }
+  if (bias.has_value() && bias->defined()) {
+    b = bias->contiguous();
+    a.bias = b.data_ptr();
+    a.b_dtype = to_dt(b.scalar_type());
+  }
+  a.eps = static_cast<float>(eps);
+  a.out = out.data_ptr();
+  a.out_row_stride = cols;
+  a.out_dtype = a.x_dtype;
+  a.mean_out = mean.data_ptr<float>();
+  a.rstd_out = rstd.data_ptr<float>();
+  check(b200k_rownorm(&a, stream_of(x)), "layer_norm");
+  return {out, mean, rstd};
+}
+
+at::Tensor softmax_impl(const at::Tensor& x_in, int64_t dim, bool half_to_float, bool log) {
+  TORCH_CHECK(x_in.is_cuda(), "b200::softmax: x must be a CUDA tensor");
+  const int64_t nd = x_in.dim();
+  TORCH_CHECK(nd >= 1 && (dim == -1 || dim == nd - 1), "b200::softmax: only the last dim is supported");
+  c10::cuda::CUDAGuard guard(x_in.device());
+  const at::Tensor x = x_in.stride(-1) == 1 ? x_in : x_in.contiguous();
+  int64_t rows, cols, rs;
+  rows_of(x, rows, cols, rs);
+  const at::ScalarType odt = half_to_float ? at::kFloat : x.scalar_type();
+  at::Tensor out = at::empty(x.sizes(), x.options().dtype(odt));
+  B200kSoftmaxArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.rows = rows;
+  a.cols = cols;
+  a.x = x.data_ptr();
+  a.x_row_stride = rs;
+  a.x_dtype = to_dt(x.scalar_type());
+  a.log_softmax = log ? 1 : 0;
+  a.out = out.data_ptr();
+  a.out_row_stride = cols;
+  a.out_dtype = to_dt(odt);
+  check(b200k_softmax(&a, stream_of(x)), log ? "log_softmax" : "softmax");
+  return out;
+}
+
+at::Tensor softmax(const at::Tensor& x, int64_t dim, bool half_to_float) {
+  return softmax_impl(x, dim, half_to_float, false);
+}
+at::Tensor log_softmax(const at::Tensor& x, int64_t dim, bool half_to_float) {
+  return softmax_impl(x, dim, half_to_float, true);
+}
+
+}  // namespace
+
+TORCH_LIBRARY(b200, m) {
+  m.def("pointwise(Tensor[] inputs, int[] code, float[] imm, int[] out_shape, ScalarType out_dtype) -> Tensor");
+  m.def(
+      "gemm_epilogue(Tensor a, Tensor b, Tensor[] extras, int[] code, float[] imm, int[] out_shape, "
+      "ScalarType out_dtype) -> Tensor");
+  m.def("rms_norm(Tensor x, Tensor? weight, float eps, int flags, ScalarType out_dtype) -> Tensor");
+  m.def("rms_norm_swiglu(Tensor x, Tensor? weight, float eps, int flags, ScalarType out_dtype) -> Tensor");
+  m.def(
+      "layer_norm(Tensor x, int[] normalized_shape, Tensor? weight, Tensor? bias, float eps) -> "
+      "(Tensor, Tensor, Tensor)");
+  m.def("softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
+  m.def("log_softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
+  m.def("gemm_status(int device, bool reset) -> int", &gemm_status);
+}
+
+TORCH_LIBRARY_IMPL(b200, CUDA, m) {
+  m.impl("pointwise", &pointwise);
+  m.impl("gemm_epilogue", &gemm_epilogue);
+  m.impl("rms_norm", &rms_norm);
+  m.impl("rms_norm_swiglu", &rms_norm_swiglu);
+  m.impl("layer_norm", &layer_norm);
+  m.impl("softmax", &softmax);
+  m.impl("log_softmax", &log_softmax);
+}
+
