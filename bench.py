@@ -1,0 +1,417 @@
+"""Benchmark: fused GEMM + epilogue sweep on B200 (the headline workload).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload sweep|chain|vit|llama]
+
+One step of the default workload ("gemm_epilogue_sweep") runs the fused bf16
+GEMM sweep once: Y = act(X W^T + b) + R for act in {none, gelu, silu} and
+(M, N, K) in {512^3, 4096^3, 8192^3, (16384, 4096, 14336)} -- twelve launches
+of the library's tcgen05 GEMM kernel with the epilogue fused.  `value` is the
+sweep's total FLOPs (2MNK per GEMM) / device time, inputs resident in HBM.
+`e2e` is the same metric through the public API (torch.compile with
+custom_backend) with X and R copied in from pinned host memory and Y copied
+back inside the timed region.
+
+Multi-GPU: one process per GPU (torchrun), each GPU runs the full sweep as an
+independent replica (weak scaling, no data-path collective); a gloo process
+group carries only the barrier and the max-over-ranks time.
+
+--impl reference times the CPU implementation of the same path on the host
+cores: the oracle restatement of the reference kernels' arithmetic (numpy
+fp32 GEMM + epilogue), on a bounded row sample of every sweep GEMM.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "torch-compile-backend_b200"))
+sys.path.insert(0, ROOT)
+
+SWEEP = [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 14336)]
+ACTS = ["none", "gelu", "silu"]
+DOMINANT = (16384, 4096, 14336)
+L2_BYTES = 126 * 1024 * 1024
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic(name: str):
+    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md
+    (line 'dram_bytes_per_launch: <int>'), or None."""
+    p = os.path.join(ROOT, "profiles", name + ".md")
+    if not os.path.exists(p):
+        return None
+    for line in open(p):
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks/throttle reasons while the timed region runs."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict | None:
+        rows = []
+        for line in self.lines:
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i, v in enumerate(r[3]) if v.lower() == "active"})
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": reasons}
+
+
+# --------------------------------------------------------------- distributed
+class Dist:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.pg = False
+        if self.world > 1:
+            import datetime
+
+            import torch.distributed as dist
+
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.barrier()
+
+    def max(self, v: float) -> float:
+        if not self.pg:
+            return v
+        import torch.distributed as dist
+
+        t = torch.tensor([v], dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+# --------------------------------------------------------------- sweep
+def _sweep_problems(dev, gen):
+    from bench_models import GemmEpilogueBlock, init_sweep_block
+
+    probs = []
+    for (M, N, K) in SWEEP:
+        x = (0.02 * torch.randn(M, K, device=dev, generator=gen)).to(torch.bfloat16)
+        r = (0.02 * torch.randn(M, N, device=dev, generator=gen)).to(torch.bfloat16)
+        for act in ACTS:
+            blk = GemmEpilogueBlock(K, N, act)
+            init_sweep_block(blk, torch.Generator().manual_seed(len(probs)))
+            blk = blk.to(dev, torch.bfloat16).eval()
+            probs.append({"shape": (M, N, K), "act": act, "x": x, "r": r, "block": blk})
+    return probs
+
+
+def _pass_program(block, x, r):
+    """The (code, imm) the FX passes build for this block: compile it with a
+    backend that keeps the rewritten graph and read the fused node's args."""
+    from torch._decomp import get_decompositions
+    from torch._dynamo.backends.common import aot_autograd
+
+    from compiler import backend as B
+
+    found = []
+
+    def comp(gm, example_inputs):
+        f = B.compiler(gm, example_inputs)
+        found.extend(n for n in gm.graph.nodes if n.op == "call_function"
+                     and n.target == torch.ops.b200.gemm_epilogue.default)
+        return f
+
+    be = aot_autograd(fw_compiler=comp, decompositions=get_decompositions([torch.ops.aten.gelu, torch.ops.aten.silu]))
+    torch._dynamo.reset()
+    with torch.no_grad():
+        torch.compile(block, backend=be)(x[:128], r[:128])
+    if len(found) != 1:
+        raise RuntimeError(f"expected one fused GEMM+epilogue node, got {len(found)}")
+    return list(found[0].args[3]), list(found[0].args[4])
+
+
+def _smi_id(local: int) -> str:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids):
+            return ids[local]
+    return str(local)
+
+
+def run_sweep(args, dist: Dist) -> dict:
+    from compiler import runtime
+    from compiler.backend import custom_backend
+
+    runtime.load()
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    probs = _sweep_problems(dev, gen)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+
+    # Device-resident step: the exact op the compiled graph calls.
+    outs = []
+    for p in probs:
+        M, N, K = p["shape"]
+        code, imm = _pass_program(p["block"], p["x"], p["r"])
+        lin = p["block"].lin
+        p["call"] = (lambda x=p["x"], w=lin.weight, b=lin.bias, r=p["r"], c=code, i=imm, s=[M, N]:
+                     torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], c, i, s, torch.bfloat16))
+    flops = sum(2.0 * p["shape"][0] * p["shape"][1] * p["shape"][2] for p in probs)
+
+    def step(record=None):
+        for j, p in enumerate(probs):
+            if record is not None:
+                record[j][0].record()
+            out = p["call"]()
+            if record is not None:
+                record[j][1].record()
+        return out
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    ev = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in probs]
+          for _ in range(args.steps)]
+    torch.cuda.synchronize()
+    dist.barrier()
+    with ClockSampler(_smi_id(dist.local)) as clk:
+        torch.cuda.synchronize()
+        for k in range(args.steps):
+            flush.zero_()  # L2 flush between steps (outside the per-launch events)
+            step(ev[k])
+        torch.cuda.synchronize()
+    dist.barrier()
+    per = [[ev[k][j][0].elapsed_time(ev[k][j][1]) for k in range(args.steps)] for j in range(len(probs))]
+    step_ms = sum(sum(per[j][k] for j in range(len(probs))) for k in range(args.steps)) / args.steps
+    step_ms = dist.max(step_ms)
+
+    # Correctness spot check of the timed op against the fp32 reference (8 rows).
+    p = probs[4]
+    lin = p["block"].lin
+    y = p["call"]()
+    ref = torch.nn.functional.gelu(p["x"][:8].float() @ lin.weight.float().t() + lin.bias.float()) + p["r"][:8].float()
+    err = ((y[:8].float() - ref).abs().max() / ref.abs().max()).item()
+
+    # End to end through torch.compile(custom_backend) with host buffers.
+    torch._dynamo.reset()
+    compiled = [torch.compile(p["block"], backend=custom_backend) for p in probs]
+    host = []
+    for p in probs:
+        M, N, K = p["shape"]
+        host.append((p["x"].cpu().pin_memory(), p["r"].cpu().pin_memory(),
+                     torch.empty(M, N, dtype=torch.bfloat16).pin_memory()))
+    h2d = sum(hx.numel() * 2 + hr.numel() * 2 for hx, hr, _ in host)
+    d2h = sum(hy.numel() * 2 for _, _, hy in host)
+
+    def e2e_step():
+        for (hx, hr, hy), f in zip(host, compiled):
+            x = hx.to(dev, non_blocking=True)
+            r = hr.to(dev, non_blocking=True)
+            with torch.no_grad():
+                y = f(x, r)
+            hy.copy_(y, non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e2e_ms = dist.max(e0.elapsed_time(e1) / args.steps)
+
+    peaks, src = load_peaks()
+    dom = [j for j, p in enumerate(probs) if p["shape"] == DOMINANT and p["act"] == "gelu"][0]
+    M, N, K = DOMINANT
+    dom_ms = statistics.mean(per[dom])
+    achieved = 2.0 * M * N * K / (dom_ms * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    sweep_detail = []
+    for (M, N, K) in SWEEP:
+        for act in ACTS:
+            j = [i for i, p in enumerate(probs) if p["shape"] == (M, N, K) and p["act"] == act][0]
+            ms = statistics.mean(per[j])
+            sweep_detail.append({"M": M, "N": N, "K": K, "act": act, "ms": round(ms, 4),
+                                 "tflops": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1)})
+    n = dist.world
+    return {
+        "metric": "fused GEMM+epilogue TFLOP/s",
+        "value": round(n * flops / (step_ms * 1e-3) / 1e12, 2),
+        "unit": "TFLOP/s",
+        "n_gpus": n,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded N(0,0.02) X/W/R, N(0,0.01) b)",
+        "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS,
+                   "epilogue": "act(X W^T + b) + R, bf16 in/out, fp32 accumulate",
+                   "l2": "256 MB flush between steps (outside the per-launch events)",
+                   "parallelism": f"replicas x{n}"},
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 3), "peak_source": f"{src} bf16_tflops_sustained",
+                     "frac_of_burst": round(achieved / peaks["bf16_tflops"], 3),
+                     "kernel": "gemm_epilogue_kernel 16384x4096x14336 gelu",
+                     "traffic": profile_traffic("gemm_epilogue_16384x4096x14336")},
+        "e2e": {"value": round(n * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+        "gpu_launches": args.steps * len(probs),
+        "clocks": clk.summary(),
+        "sweep": sweep_detail,
+        "spot_check_max_rel_err": round(err, 5),
+    }
+
+
+# --------------------------------------------------------------- CPU (oracle) leg
+def cpu_sweep(rows: int, reps: int) -> dict:
+    """The oracle's GEMM + epilogue (numpy fp32, every host core via BLAS) on
+    the first `rows` rows of every sweep GEMM."""
+    import numpy as np
+
+    import oracle
+
+    rng = np.random.default_rng(0)
+    gelu = [["mul.Tensor", [["acc"], 0.5]], ["mul.Tensor", [["acc"], 0.7071067811865476]],
+            ["erf.default", [["node", 1]]], ["add.Tensor", [["node", 2], 1.0]],
+            ["mul.Tensor", [["node", 0], ["node", 3]]]]
+    silu = [["sigmoid.default", [["acc"]]], ["mul.Tensor", [["acc"], ["node", 0]]]]
+    work = []
+    for (M, N, K) in SWEEP:
+        m = min(rows, M)
+        x = oracle.round_bf16((0.02 * rng.standard_normal((m, K))).astype(np.float32))
+        w = oracle.round_bf16((0.02 * rng.standard_normal((K, N))).astype(np.float32))
+        b = oracle.round_bf16((0.01 * rng.standard_normal(N)).astype(np.float32))
+        r = oracle.round_bf16((0.02 * rng.standard_normal((m, N))).astype(np.float32))
+        for act, spec in (("none", []), ("gelu", gelu), ("silu", silu)):
+            s = list(spec) + [["add.Tensor", [["node", len(spec) - 1] if spec else ["acc"], ["in", 1]]]]
+            work.append((x, w, b, r, s, 2.0 * m * N * K))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for x, w, b, r, s, _ in work:
+            oracle.gemm_epilogue(x, w, s, [b, r], "bfloat16", bias=b)
+    dt = time.perf_counter() - t0
+    flops = reps * sum(f for *_, f in work)
+    return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"first {rows} rows of each of the 12 sweep GEMMs, x{reps}; {dt:.1f} s",
+            "seconds": round(dt, 2)}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep"])
+    ap.add_argument("--cpu-rows", type=int, default=256)
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+
+    dist_env_rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if dist_env_rank != 0:
+            return
+        base = cpu_sweep(args.cpu_rows, max(1, args.steps // 5))
+        line = {"impl": "reference", "metric": "fused GEMM+epilogue TFLOP/s", "value": base["value"],
+                "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic", "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS},
+                "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line))
+        return
+
+    dist = Dist()
+    try:
+        res = run_sweep(args, dist)
+        if dist.rank == 0:
+            if dist.world == 1:
+                base = cpu_sweep(args.cpu_rows, 1)
+                res["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            print(json.dumps(res))
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,100 @@
+"""CPU checks of the C ABI: the library loads without a GPU, exports every
+function include/b200k.h declares, and the ctypes mirror has the C layout."""
+import ctypes
+import os
+import re
+import subprocess
+import tempfile
+
+import pytest
+
+from compiler import runtime
+from compiler.runtime import cabi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "b200k.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(b200k_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_header_declarations_are_exported():
+    lib = ctypes.CDLL(runtime.LIB_PATH)
+    names = declared_functions()
+    assert len(names) >= 9
+    for name in names:
+        assert hasattr(lib, name), f"{name} declared in b200k.h but not exported"
+    assert sorted(cabi.EXPORTED) == sorted(n for n in names if n in cabi.EXPORTED)
+
+
+def test_library_answers_without_gpu():
+    lib = cabi.library()
+    assert lib.b200k_version() == 1
+    assert lib.b200k_status_string(6).decode().startswith("device-side wait")
+    n = lib.b200k_gemm_num_configs()
+    assert n >= 2
+    bm, bn, bk, st = (ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int())
+    assert lib.b200k_gemm_config_info(0, ctypes.byref(bm), ctypes.byref(bn), ctypes.byref(bk), ctypes.byref(st)) == 0
+    assert (bm.value, bk.value) == (128, 64) and bn.value in (128, 256)
+    assert lib.b200k_gemm_config_info(n, None, None, None, None) == 1  # B200K_ERR_ARG
+
+
+def test_host_side_errors_need_no_gpu():
+    """Argument errors are caught before any CUDA call."""
+    lib = cabi.library()
+    assert lib.b200k_pointwise(None, None) == 1
+    a = cabi.PointwiseArgs()
+    a.n_inputs = 0
+    assert lib.b200k_pointwise(ctypes.byref(a), None) == 1
+    g = cabi.GemmArgs()
+    assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 1  # null pointers
+    g.a = g.b = g.out = 16
+    g.M, g.N, g.K = 4, 4, 0
+    assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 3  # K == 0
+    g.K = 8
+    g.ab_dtype = cabi.F32
+    assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 4  # fp32 operands unsupported
+    g.ab_dtype = cabi.BF16
+    g.out_dtype = cabi.BF16
+    g.program = cabi.make_program([999], [0.0])
+    assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 7  # malformed program
+    r = cabi.RowNormArgs()
+    assert lib.b200k_rownorm(ctypes.byref(r), None) == 1
+
+
+STRUCTS = {
+    "B200kInstr": (cabi.Instr, ["code", "imm"]),
+    "B200kProgram": (cabi.Program, ["n", "ins"]),
+    "B200kTensorRef": (cabi.TensorRef, ["ptr", "dtype", "strides"]),
+    "B200kPointwiseArgs": (cabi.PointwiseArgs, ["rank", "n_inputs", "sizes", "inputs", "out", "out_dtype", "program"]),
+    "B200kEpiOperand": (cabi.EpiOperand, ["ptr", "dtype", "stride_m", "stride_n"]),
+    "B200kGemmArgs": (cabi.GemmArgs, ["M", "a", "b_stride_n", "ab_dtype", "out", "n_extras", "tile_config",
+                                      "extras", "program", "status", "timeout_ns"]),
+    "B200kRowNormArgs": (cabi.RowNormArgs, ["rows", "x", "kind", "weight", "flags", "bias", "eps", "out",
+                                            "out_dtype", "mean_out", "rstd_out"]),
+    "B200kSoftmaxArgs": (cabi.SoftmaxArgs, ["rows", "x", "log_softmax", "out", "out_dtype"]),
+}
+
+
+def test_ctypes_layout_matches_c():
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "b200k.h"', "int main(void) {"]
+    for cname, (_, fields) in STRUCTS.items():
+        lines.append(f'  printf("{cname} size %zu\\n", sizeof({cname}));')
+        for f in fields:
+            lines.append(f'  printf("{cname} {f} %zu\\n", offsetof({cname}, {f}));')
+    lines.append("  return 0; }")
+    with tempfile.TemporaryDirectory() as d:
+        src = os.path.join(d, "layout.c")
+        exe = os.path.join(d, "layout")
+        open(src, "w").write("\n".join(lines))
+        r = subprocess.run(["gcc", "-I", os.path.dirname(HEADER), src, "-o", exe], capture_output=True, text=True)
+        if r.returncode != 0:
+            pytest.fail(r.stderr)
+        out = subprocess.run([exe], capture_output=True, text=True, check=True).stdout.split("\n")
+    for line in filter(None, out):
+        cname, field, value = line.split()
+        cls = STRUCTS[cname][0]
+        got = ctypes.sizeof(cls) if field == "size" else getattr(cls, field).offset
+        assert got == int(value), f"{cname}.{field}: ctypes {got} vs C {value}"

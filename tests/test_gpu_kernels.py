@@ -1,0 +1,331 @@
+"""GPU parity of the sm_100a kernels, called through the C ABI (ctypes), against
+the oracle and the reference kernels' recorded outputs.
+
+Tolerances: fp32 pointwise 1e-5 relative (+1e-6 absolute); fp16/bf16 results
+one rounding of the output dtype; GEMM + epilogue 2e-2 relative to an fp32
+reference (scaled by the output's magnitude), as the task's parity bar states.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import spec_graph
+from compiler import runtime
+from compiler.optimization.program import OP, compile_group
+from compiler.runtime import cabi
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+with open(os.path.join(os.path.dirname(__file__), "golden", "reference_kernels.json")) as _f:
+    _META = json.load(_f)
+GOLDEN_IDS = [i for i, k in enumerate(_META["kernels"]) if k["calls"]]
+
+GELU_ERF = [["mul.Tensor", [["acc"], 0.5]], ["mul.Tensor", [["acc"], 0.7071067811865476]], ["erf.default", [["node", 1]]],
+            ["add.Tensor", [["node", 2], 1.0]], ["mul.Tensor", [["node", 0], ["node", 3]]]]
+SILU = [["sigmoid.default", [["acc"]]], ["mul.Tensor", [["acc"], ["node", 0]]]]
+GELU_TANH = [["mul.Tensor", [["acc"], ["acc"]]], ["mul.Tensor", [["node", 0], ["acc"]]],
+             ["mul.Tensor", [["node", 1], 0.044715]], ["add.Tensor", [["acc"], ["node", 2]]],
+             ["mul.Tensor", [["node", 3], 0.7978845608028654]], ["mul.Tensor", [["acc"], 0.5]],
+             ["tanh.default", [["node", 4]]], ["add.Tensor", [["node", 6], 1.0]],
+             ["mul.Tensor", [["node", 5], ["node", 7]]]]
+ACTS = {"none": [], "gelu": GELU_ERF, "silu": SILU, "gelu_tanh": GELU_TANH}
+
+
+def _tdt(name):
+    return getattr(torch, name)
+
+
+def _assert_close(got: torch.Tensor, want: np.ndarray, rtol: float, atol: float):
+    np.testing.assert_allclose(got.float().cpu().numpy(), want, rtol=rtol, atol=atol)
+
+
+def _gemm_tol(want: np.ndarray) -> tuple[float, float]:
+    return 2e-2, 2e-2 * float(np.abs(want).max() + 1e-6)
+
+
+def epilogue_program(act: str, residual: bool, bias: bool = True):
+    """Program for out = act(acc [+ bias]) [+ residual] with extras (bias, residual)."""
+    spec = [list(s) for s in ACTS[act]]
+    n_in = (1 if bias else 0) + (1 if residual else 0)
+    if residual:
+        last = ["node", len(spec) - 1] if spec else ["acc"]
+        spec = spec + [["add.Tensor", [last, ["in", n_in - 1]]]]
+    if not spec:
+        spec = [["add.Tensor", [["acc"], 0.0]]] if not bias else []
+    nodes, ops = spec_graph.build(spec, n_in, with_acc=True) if spec else (None, None)
+    if spec:
+        pro = [("ADD", ops[1])] if bias else None
+        prog = compile_group(nodes, ops, prologue=pro, prologue_target=ops[0])
+        return prog.code, prog.imm, spec
+    # bias only: acc + bias
+    return [OP["MOV"] * 10, OP["ADD"] * 10 + 1], [0.0, 0.0], []
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib():
+    runtime.load()
+    cabi.library()
+
+
+@pytest.mark.parametrize("k", [i for i in GOLDEN_IDS if _META["kernels"][i]["kind"] == "pointwise"])
+def test_golden_pointwise_kernel(golden, k):
+    meta, arrays = golden
+    ent = meta["kernels"][k]
+    nodes, ops = spec_graph.build(ent["spec"], ent["n_inputs"])
+    prog = compile_group(nodes, ops)
+    ins = [torch.from_numpy(arrays[f"k{k}_in{i}"]).to(DEV, _tdt(ent["in_dtypes"][i])) for i in range(ent["n_inputs"])]
+    out = torch.empty(ent["out_shape"], device=DEV, dtype=_tdt(ent["out_dtype"]))
+    cabi.pointwise(ins, prog.code, prog.imm, out)
+    torch.cuda.synchronize()
+    rtol, atol = (1e-5, 1e-6) if ent["out_dtype"] == "float32" else (2e-3, 1e-3)
+    _assert_close(out, arrays[f"k{k}_out"], rtol, atol)
+    # the oracle agrees on the same inputs
+    want = oracle.eval_group(ent["spec"], [arrays[f"k{k}_in{i}"] for i in range(ent["n_inputs"])],
+                             tuple(ent["out_shape"]), ent["out_dtype"])
+    _assert_close(out, want, rtol, atol)
+
+
+@pytest.mark.parametrize("k", [i for i in GOLDEN_IDS if _META["kernels"][i]["kind"] == "gemm_epilogue"])
+@pytest.mark.parametrize("b_layout", ["k_major", "n_major"])
+def test_golden_gemm_epilogue_kernel(golden, k, b_layout):
+    meta, arrays = golden
+    ent = meta["kernels"][k]
+    nodes, ops = spec_graph.build(ent["spec"], ent["n_inputs"], with_acc=True)
+    pro = [("ADD", ops[1])] if ent["bias_first"] else None
+    prog = compile_group(nodes, ops, prologue=pro, prologue_target=ops[0])
+    dt = _tdt(ent["ab_dtype"])
+    a = torch.from_numpy(arrays[f"k{k}_a"]).to(DEV, dt)
+    bnp = arrays[f"k{k}_b"]
+    b = torch.from_numpy(bnp.T.copy()).to(DEV, dt).t() if b_layout == "k_major" else torch.from_numpy(bnp).to(DEV, dt)
+    extras = [torch.from_numpy(arrays[f"k{k}_in{i}"]).to(DEV, _tdt(ent["in_dtypes"][i])) for i in range(ent["n_inputs"])]
+    out = torch.empty(ent["out_shape"], device=DEV, dtype=_tdt(ent["out_dtype"]))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cabi.gemm_epilogue(a, b, extras, prog.code, prog.imm, out, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    _assert_close(out, arrays[f"k{k}_out"], 2e-3, 2e-3)
+
+
+SWEEP = [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 14336)]
+
+
+@pytest.mark.parametrize("shape", SWEEP)
+@pytest.mark.parametrize("act", ["none", "gelu", "silu"])
+def test_gemm_sweep_configs(shape, act):
+    """The fused GEMM sweep at its full sizes, Y = act(X W^T + b) + R in bf16;
+    checked on 192 sampled rows against the fp32 oracle."""
+    M, N, K = shape
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = (0.02 * torch.randn(M, K, device=DEV, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn(N, K, device=DEV, generator=g)).to(torch.bfloat16)
+    b = (0.01 * torch.randn(N, device=DEV, generator=g)).to(torch.bfloat16)
+    r = (0.02 * torch.randn(M, N, device=DEV, generator=g)).to(torch.bfloat16)
+    code, imm, spec = epilogue_program(act, residual=True)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, status=status)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(1))[:192].sort().values
+    rows[0], rows[-1] = 0, M - 1
+    xs = x[rows.to(DEV)].float().cpu().numpy()
+    want = oracle.gemm_epilogue(xs, w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), r[rows.to(DEV)].float().cpu().numpy()], "bfloat16",
+                                bias=b.float().cpu().numpy())
+    _assert_close(out[rows.to(DEV)], want, *_gemm_tol(want))
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 8, 8), (37, 72, 24), (128, 256, 64), (130, 260, 72), (300, 100, 136),
+                                   (257, 1000, 768), (64, 4096, 1024)])
+@pytest.mark.parametrize("config", [0, 1])
+@pytest.mark.parametrize("ab", ["bfloat16", "float16"])
+def test_gemm_edge_shapes(M, N, K, config, ab):
+    """Ragged M/N/K (partial tiles, K tail inside a 64-wide block, M < 128,
+    N whose rows are not 16-byte multiples -> direct-store path), both tile
+    configs, both operand dtypes, gelu-tanh + bias + residual."""
+    dt = _tdt(ab)
+    g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
+    x = torch.randn(M, K, device=DEV, generator=g).to(dt)
+    w = torch.randn(N, K, device=DEV, generator=g).to(dt)
+    b = torch.randn(N, device=DEV, generator=g).to(dt)
+    r = torch.randn(M, N, device=DEV, generator=g).to(dt)
+    code, imm, spec = epilogue_program("gelu_tanh", residual=True)
+    out = torch.empty(M, N, device=DEV, dtype=dt)
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=config)
+    torch.cuda.synchronize()
+    want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), r.float().cpu().numpy()], ab, bias=b.float().cpu().numpy())
+    _assert_close(out, want, *_gemm_tol(want))
+
+
+@pytest.mark.parametrize("out_dtype", ["float32", "float16"])
+def test_gemm_extras_broadcast_and_strided(out_dtype):
+    """Epilogue operands of every layout: [M,1] column, 0-d scalar, fp32 row
+    vector, a transposed [M,N] view; N-major B; fp32 output."""
+    M, N, K = 200, 320, 96
+    g = torch.Generator(device=DEV).manual_seed(3)
+    x = torch.randn(M, K, device=DEV, generator=g).half()
+    bm = torch.randn(K, N, device=DEV, generator=g).half()  # N-major B
+    col = torch.randn(M, 1, device=DEV, generator=g)
+    scal = torch.tensor(1.5, device=DEV)
+    rowv = torch.randn(N, device=DEV, generator=g)
+    rt = torch.randn(N, M, device=DEV, generator=g).half().t()
+    spec = [["mul.Tensor", [["acc"], ["in", 0]]], ["add.Tensor", [["node", 0], ["in", 1]]],
+            ["maximum.default", [["node", 1], ["in", 2]]], ["sub.Tensor", [["node", 2], ["in", 3]]]]
+    nodes, ops = spec_graph.build(spec, 4, with_acc=True)
+    prog = compile_group(nodes, ops)
+    out = torch.empty(M, N, device=DEV, dtype=_tdt(out_dtype))
+    cabi.gemm_epilogue(x, bm, [col, scal, rowv, rt], prog.code, prog.imm, out)
+    torch.cuda.synchronize()
+    want = oracle.gemm_epilogue(x.float().cpu().numpy(), bm.float().cpu().numpy(), spec,
+                                [t.float().cpu().numpy() for t in (col, scal, rowv, rt)], out_dtype)
+    _assert_close(out, want, *_gemm_tol(want))
+
+
+def test_gemm_repeated_calls_reuse_nothing_stale():
+    """Two different problems back to back on one stream give independent results."""
+    for M, N, K in [(256, 512, 128), (1024, 256, 64)]:
+        x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+        w = torch.randn(N, K, device=DEV).to(torch.bfloat16)
+        out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+        cabi.gemm_epilogue(x, w.t(), [], [], [], out)
+        torch.cuda.synchronize()
+        want = x.float().cpu().numpy() @ w.float().cpu().numpy().T
+        _assert_close(out, oracle.round_to(want, "bfloat16"), *_gemm_tol(want))
+
+
+def test_gemm_rejects_bad_layout():
+    """A with a non-unit K stride is refused with an error code, not computed wrongly."""
+    x = torch.randn(64, 64, device=DEV).to(torch.bfloat16).t()  # strides (1, 64)
+    w = torch.randn(56, 64, device=DEV).to(torch.bfloat16)
+    out = torch.empty(64, 56, device=DEV, dtype=torch.bfloat16)
+    with pytest.raises(cabi.CError) as e:
+        cabi.gemm_epilogue(x, w.t(), [], [], [], out)
+    assert e.value.code == 4
+
+
+# ------------------------------------------------------------- pointwise
+def test_pointwise_broadcast_strided_and_dtypes():
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(33, 48, device=DEV, generator=g)
+    xt = torch.randn(48, 33, device=DEV, generator=g).t()  # transposed view
+    row = torch.randn(48, device=DEV, generator=g).half()
+    col = torch.randn(33, 1, device=DEV, generator=g).to(torch.bfloat16)
+    mask = torch.rand(33, 48, device=DEV, generator=g) > 0.5
+    idx = torch.randint(-3, 3, (33, 48), device=DEV, generator=g, dtype=torch.int32)
+    spec = [["mul.Tensor", [["in", 0], ["in", 1]]], ["add.Tensor", [["node", 0], ["in", 2]]],
+            ["sub.Tensor", [["node", 1], ["in", 3]]], ["mul.Tensor", [["node", 2], ["in", 4]]],
+            ["add.Tensor", [["node", 3], ["in", 5]]]]
+    nodes, ops = spec_graph.build(spec, 6)
+    prog = compile_group(nodes, ops)
+    ins = [x, xt, row, col, mask, idx]
+    for od in ("float32", "float64", "bfloat16"):
+        out = torch.empty(33, 48, device=DEV, dtype=_tdt(od))
+        cabi.pointwise(ins, prog.code, prog.imm, out)
+        torch.cuda.synchronize()
+        want = oracle.eval_group(spec, [t.float().cpu().numpy() for t in ins], (33, 48), od)
+        tol = (1e-5, 1e-6) if od != "bfloat16" else (1e-2, 1e-2)
+        _assert_close(out, want, *tol)
+
+
+@pytest.mark.parametrize("shape", [(1,), (7,), (3, 5, 7), (2, 3, 4, 5, 6, 8), (16384, 8192)])
+def test_pointwise_shapes(shape):
+    x = torch.randn(shape, device=DEV).to(torch.bfloat16)
+    y = torch.randn(shape[-1:], device=DEV).to(torch.bfloat16)
+    spec = [["sigmoid.default", [["in", 0]]], ["mul.Tensor", [["in", 0], ["node", 0]]],
+            ["mul.Tensor", [["node", 1], ["in", 1]]]]
+    nodes, ops = spec_graph.build(spec, 2)
+    prog = compile_group(nodes, ops)
+    out = torch.empty(shape, device=DEV, dtype=torch.bfloat16)
+    cabi.pointwise([x, y], prog.code, prog.imm, out)
+    torch.cuda.synchronize()
+    if x.numel() > 1 << 20:  # full size: property check on a row sample
+        sel = slice(0, 64)
+        want = oracle.eval_group(spec, [x[sel].float().cpu().numpy(), y.float().cpu().numpy()],
+                                 tuple(x[sel].shape), "bfloat16")
+        _assert_close(out[sel], want, 1e-2, 1e-2)
+        assert torch.isfinite(out).all()
+    else:
+        want = oracle.eval_group(spec, [x.float().cpu().numpy(), y.float().cpu().numpy()], shape, "bfloat16")
+        _assert_close(out, want, 1e-2, 1e-2)
+
+
+def test_pointwise_empty_is_noop():
+    x = torch.empty(0, 5, device=DEV)
+    out = torch.empty(0, 5, device=DEV)
+    cabi.pointwise([x], [OP["MOV"] * 10], [0.0], out)
+
+
+# ------------------------------------------------------------- row kernels
+@pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768)])
+def test_rms_norm_swiglu(rows, cols):
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = torch.randn(rows, cols, device=DEV, generator=g).to(torch.bfloat16)
+    w = (1 + 0.02 * torch.randn(cols, device=DEV, generator=g)).to(torch.bfloat16)
+    out = torch.empty(rows, cols // 2, device=DEV, dtype=torch.bfloat16)
+    cabi.rownorm(x, cabi.ROW_RMSNORM_SWIGLU, w, None, 1e-6, 7, out)
+    torch.cuda.synchronize()
+    sel = slice(0, min(rows, 256))
+    want = oracle.rms_norm_swiglu(x[sel].float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, 7, "bfloat16",
+                                  "bfloat16")
+    _assert_close(out[sel], want, 1e-2, 1e-2)
+    if rows > 256:  # the last rows too
+        want = oracle.rms_norm_swiglu(x[-64:].float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, 7, "bfloat16",
+                                      "bfloat16")
+        _assert_close(out[-64:], want, 1e-2, 1e-2)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
+@pytest.mark.parametrize("cols", [2048, 768, 100])
+def test_rms_norm(dtype, cols):
+    dt = _tdt(dtype)
+    x = torch.randn(67, cols, device=DEV).to(dt)
+    w = (1 + 0.1 * torch.randn(cols, device=DEV)).to(dt)
+    flags = 0 if dtype == "float32" else 1
+    out = torch.empty_like(x)
+    rstd = torch.empty(67, device=DEV)
+    cabi.rownorm(x, cabi.ROW_RMSNORM, w, None, 1e-5, flags, out, rstd_out=rstd)
+    torch.cuda.synchronize()
+    want = oracle.rms_norm(x.float().cpu().numpy(), w.float().cpu().numpy(), 1e-5, flags, dtype, dtype)
+    tol = (1e-5, 1e-5) if dtype == "float32" else (1e-2, 1e-2)
+    _assert_close(out, want, *tol)
+
+
+@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50)])
+def test_layer_norm(rows, cols):
+    x = torch.randn(rows, cols, device=DEV).to(torch.bfloat16)
+    w = torch.randn(cols, device=DEV).to(torch.bfloat16)
+    b = torch.randn(cols, device=DEV).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    mean = torch.empty(rows, device=DEV)
+    rstd = torch.empty(rows, device=DEV)
+    cabi.rownorm(x, cabi.ROW_LAYERNORM, w, b, 1e-6, 0, out, mean_out=mean, rstd_out=rstd)
+    torch.cuda.synchronize()
+    sel = slice(0, 500)
+    o, m, r = oracle.layer_norm(x[sel].float().cpu().numpy(), w.float().cpu().numpy(), b.float().cpu().numpy(), 1e-6,
+                                "bfloat16")
+    _assert_close(out[sel], o, 1e-2, 2e-2)
+    _assert_close(mean[sel], m[:, 0], 1e-5, 1e-5)
+    _assert_close(rstd[sel], r[:, 0], 1e-4, 1e-5)
+
+
+@pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768)])
+@pytest.mark.parametrize("log", [False, True])
+def test_softmax(rows, cols, log):
+    g = torch.Generator(device=DEV).manual_seed(0)
+    x = (2 * torch.randn(rows, cols, device=DEV, generator=g)).to(torch.bfloat16)
+    out = torch.empty_like(x)
+    cabi.softmax(x, out, log=log)
+    torch.cuda.synchronize()
+    sel = slice(0, 128)
+    fn = oracle.log_softmax if log else oracle.softmax
+    want = fn(x[sel].float().cpu().numpy(), "bfloat16")
+    _assert_close(out[sel], want, 1e-2, 1e-2 if log else 1e-4)
+    if not log:  # every row sums to one
+        s = out.float().sum(-1)
+        assert torch.allclose(s, torch.ones_like(s), atol=2e-2)

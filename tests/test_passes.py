@@ -1,0 +1,237 @@
+"""CPU tests of the FX passes: grouping parity with the reference, program
+lowering (checked through the machine emulator against the reference's own
+kernel outputs), and the documented extensions."""
+import random
+
+import numpy as np
+import pytest
+import torch
+import torch.fx as fx
+import torch.nn as nn
+import torch.nn.functional as F
+
+import machine_emulator
+import oracle
+import spec_graph
+from cases import CASES, make_case
+from compiler.optimization.program import MAX_SLOTS, ProgramError, compile_group
+from helpers import fused_graphs, kernels_of
+
+aten = torch.ops.aten
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_grouping_matches_reference(golden, case):
+    """With the extensions off, the passes make the reference's decisions:
+    same kernels, same kind, same member ops, same order."""
+    meta, _ = golden
+    model, inputs = make_case(case)
+    graphs = fused_graphs(model, inputs, extensions=False)
+    ours = [(k, ops) for gm in graphs for k, ops, _ in kernels_of(gm)]
+    ref = [(k, ops) for k, ops in meta["models"][case]["groups"]]
+    assert ours == ref
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_operand_order_matches_reference(golden, case):
+    """Each fused node takes the reference closure's argument order:
+    (*external_inputs) for pointwise, (mat1, mat2, bias?, *externals) for GEMM."""
+    meta, _ = golden
+    model, inputs = make_case(case)
+    graphs = fused_graphs(model, inputs, extensions=False)
+    ref = [k for k in meta["kernels"] if k["case"] == case and k["calls"]]
+    ours = [n for gm in graphs for _, _, n in kernels_of(gm)]
+    assert len(ours) == len(ref)
+    for n, k in zip(ours, ref):
+        operands = n.args[0] if k["kind"] == "pointwise" else n.args[2]
+        assert len(operands) == k["n_inputs"]
+
+
+def _lower(ent):
+    if ent["kind"] == "pointwise":
+        nodes, ops = spec_graph.build(ent["spec"], ent["n_inputs"])
+        return compile_group(nodes, ops)
+    nodes, ops = spec_graph.build(ent["spec"], ent["n_inputs"], with_acc=True)
+    pro = [("ADD", ops[1])] if ent["bias_first"] else None
+    return compile_group(nodes, ops, prologue=pro, prologue_target=ops[0])
+
+
+def _golden_ids():
+    import json
+    import os
+
+    with open(os.path.join(os.path.dirname(__file__), "golden", "reference_kernels.json")) as f:
+        return [i for i, k in enumerate(json.load(f)["kernels"]) if k["calls"]]
+
+
+@pytest.mark.parametrize("k", _golden_ids())
+def test_lowered_program_reproduces_reference_kernel(golden, k):
+    meta, arrays = golden
+    ent = meta["kernels"][k]
+    prog = _lower(ent)
+    ins = [arrays[f"k{k}_in{i}"] for i in range(ent["n_inputs"])]
+    shape = tuple(ent["out_shape"])
+    if ent["kind"] == "gemm_epilogue":
+        ins = [arrays[f"k{k}_a"] @ arrays[f"k{k}_b"]] + ins
+    slots = [np.broadcast_to(x.astype(np.float32), shape) for x in ins]
+    got = oracle.round_to(machine_emulator.run(prog.code, prog.imm, slots), ent["out_dtype"])
+    rtol, atol = (1e-5, 1e-6) if ent["out_dtype"] == "float32" else (2e-3, 1e-3)
+    if ent["kind"] == "gemm_epilogue":
+        rtol, atol = max(rtol, 1e-3), max(atol, 1e-3)
+    np.testing.assert_allclose(got, arrays[f"k{k}_out"], rtol=rtol, atol=atol)
+
+
+UNARY = ["neg.default", "abs.default", "relu.default", "exp.default", "sigmoid.default", "tanh.default",
+         "erf.default"]
+BINARY = ["add.Tensor", "sub.Tensor", "mul.Tensor", "div.Tensor", "maximum.default", "minimum.default"]
+
+
+def _random_spec(rng: random.Random, n_in: int, n_ops: int):
+    spec = []
+    for j in range(n_ops):
+        def pick():
+            r = rng.random()
+            if r < 0.2:
+                return round(rng.uniform(-2, 2), 3)
+            if r < 0.55 or j == 0:
+                return ["in", rng.randrange(n_in)]
+            return ["node", rng.randrange(j)]
+
+        if rng.random() < 0.35:
+            a = pick()
+            if not isinstance(a, list):
+                a = ["in", 0]
+            spec.append([rng.choice(UNARY), [a]])
+        else:
+            a, b = pick(), pick()
+            if not isinstance(a, list) and not isinstance(b, list):
+                a = ["in", rng.randrange(n_in)]
+            spec.append([rng.choice(BINARY), [a, b]])
+    return spec
+
+
+@pytest.mark.parametrize("seed", range(60))
+def test_lowering_random_dags(seed):
+    """Random expression DAGs (shared subexpressions, operands reused,
+    scalar on either side): lowering + emulation == direct evaluation."""
+    rng = random.Random(seed)
+    n_in = rng.randint(1, 5)
+    spec = _random_spec(rng, n_in, rng.randint(2, 14))
+    nodes, ops = spec_graph.build(spec, n_in)
+    try:
+        prog = compile_group(nodes, ops)
+    except ProgramError:
+        pytest.skip("needs more than the machine's slots")
+    npr = np.random.default_rng(seed)
+    ins = [npr.standard_normal((5, 7)).astype(np.float32) for _ in range(n_in)]
+    want = oracle.eval_group(spec, ins, (5, 7), "float32")
+    got = machine_emulator.run(prog.code, prog.imm, ins)
+    np.testing.assert_allclose(got, want, rtol=1e-5, atol=1e-6, equal_nan=True)
+
+
+def test_program_rejects_too_many_live_values():
+    g = fx.Graph()
+    ins = [g.placeholder(f"x{i}") for i in range(MAX_SLOTS)]
+    # sum of pairwise products keeps every input live until the end
+    nodes = []
+    acc = None
+    for i in range(MAX_SLOTS):
+        p = g.call_function(aten.mul.Tensor, (ins[i], ins[(i + 1) % MAX_SLOTS]))
+        nodes.append(p)
+        if acc is not None:
+            acc = g.call_function(aten.add.Tensor, (acc, p))
+            nodes.append(acc)
+        else:
+            acc = p
+    extra = g.call_function(aten.mul.Tensor, (nodes[0], nodes[2]))
+    nodes.append(extra)
+    with pytest.raises(ProgramError):
+        compile_group(nodes + [g.call_function(aten.add.Tensor, (acc, extra))], ins)
+
+
+# ------------------------------------------------------------- extensions
+class RMSSwiGLU(nn.Module):
+    def __init__(self, d):
+        super().__init__()
+        self.weight = nn.Parameter(1 + 0.02 * torch.randn(d))
+
+    def forward(self, h):
+        dt = h.dtype
+        x = h.to(torch.float32)
+        x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6)
+        y = self.weight * x.to(dt)
+        g, u = y.split(y.shape[-1] // 2, dim=-1)
+        return F.silu(g) * u
+
+
+class RMSOnly(RMSSwiGLU):
+    def forward(self, h):
+        dt = h.dtype
+        x = h.to(torch.float32)
+        x = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-5)
+        return self.weight * x.to(dt)
+
+
+def _targets(gm):
+    return [n.target for n in gm.graph.nodes if n.op == "call_function"]
+
+
+def test_rmsnorm_swiglu_becomes_one_kernel():
+    (gm,) = fused_graphs(RMSSwiGLU(64).to(torch.bfloat16), (torch.randn(4, 64).to(torch.bfloat16),))
+    t = _targets(gm)
+    assert t == [torch.ops.b200.rms_norm_swiglu.default]
+    n = next(n for n in gm.graph.nodes if n.op == "call_function")
+    assert n.args[2] == pytest.approx(1e-6) and n.args[3] == 7 and n.args[4] == torch.bfloat16
+
+
+def test_rmsnorm_alone_and_fp32():
+    (gm,) = fused_graphs(RMSOnly(64).to(torch.bfloat16), (torch.randn(2, 3, 64).to(torch.bfloat16),))
+    assert _targets(gm) == [torch.ops.b200.rms_norm.default]
+    n = next(n for n in gm.graph.nodes if n.op == "call_function")
+    assert n.args[3] == 1  # round the normalised value to bf16 before the weight
+    (gm,) = fused_graphs(RMSOnly(64), (torch.randn(2, 64),))
+    n = next(n for n in gm.graph.nodes if n.op == "call_function")
+    assert n.target == torch.ops.b200.rms_norm.default and n.args[3] == 0
+
+
+def test_rmsnorm_not_fused_when_intermediate_escapes():
+    class Leak(nn.Module):
+        def forward(self, h):
+            x = h.to(torch.float32)
+            v = x.pow(2).mean(-1, keepdim=True)
+            return x * torch.rsqrt(v + 1e-6), v
+
+    (gm,) = fused_graphs(Leak(), (torch.randn(4, 64).to(torch.bfloat16),))
+    assert aten.mean.dim in _targets(gm)
+
+
+def test_layernorm_softmax_and_3d_linear_lookthrough():
+    class Blk(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln = nn.LayerNorm(64)
+            self.fc = nn.Linear(64, 128)
+            self.fc2 = nn.Linear(128, 64)
+
+        def forward(self, x):
+            return self.fc2(F.gelu(self.fc(self.ln(x)))) + x, torch.softmax(x, -1)
+
+    x = torch.randn(2, 5, 64).to(torch.bfloat16)
+    (gm,) = fused_graphs(Blk().to(torch.bfloat16), (x,))
+    t = _targets(gm)
+    assert torch.ops.b200.layer_norm.default in t
+    assert torch.ops.b200.softmax.default in t
+    assert t.count(torch.ops.b200.gemm_epilogue.default) == 2
+    assert aten.addmm.default not in t
+    # Without the extensions the reference's rules apply: no 3-d anchor, no row kernels.
+    (gm,) = fused_graphs(Blk().to(torch.bfloat16), (x,), extensions=False)
+    t = _targets(gm)
+    assert torch.ops.b200.gemm_epilogue.default not in t and aten.native_layer_norm.default in t
+
+
+def test_fp32_gemm_left_to_aten():
+    """fp32 matmuls (no TF32) stay cuBLAS; their pointwise tail is fused."""
+    model, inputs = make_case("mlp_tanh_fp32")
+    (gm,) = fused_graphs(model, inputs)
+    t = _targets(gm)
+    assert aten.addmm.default in t and torch.ops.b200.pointwise.default in t

@@ -154,7 +154,8 @@ def build_epilogue_op(group, matmul, inputs, anchor=None):
     prologue = None
     if matmul.target == aten.addmm.default:
         prologue = [("ADD", matmul.args[0])]  # acc + bias first (reference :142-143)
-    prog = compile_group(group, operands, prologue=prologue, prologue_target=anchor)
+    prog = compile_group(group, operands, prologue=prologue, prologue_target=anchor,
+                         rounding_casts=config.EXTENSIONS)
     return prog, [int(s) for s in out_meta.shape], out_meta.dtype
 
 

@@ -54,9 +54,12 @@ def _tensor_meta(node):
 
 
 def _is_float_cast(node: fx.Node) -> bool:
-    """A dtype conversion between floats that fit in fp32.  A cast below fp32
-    must end its group: only the final store rounds to the output dtype, so
-    ops after it would see the unrounded value (reference :67-79)."""
+    """A dtype conversion between floats that fit in fp32.  In the reference a
+    cast below fp32 must end its group: only the final store rounds, so ops
+    after it would see the unrounded value (reference :67-79).  With the
+    extensions on, the kernel rounds at the cast itself (ROUND_BF16/F16), so
+    such a cast may sit inside a group and bf16 chains like
+    cast -> gelu -> cast -> +residual stay one kernel with eager's rounding."""
     src, dst = _tensor_meta(node.args[0]), _tensor_meta(node)
     return (
         set(node.kwargs) == {"dtype"}
@@ -64,7 +67,11 @@ def _is_float_cast(node: fx.Node) -> bool:
         and dst is not None
         and src.is_floating_point()
         and torch.float64 not in (src.dtype, dst.dtype)
-        and (dst.dtype == torch.float32 or not any(_is_fusible(u) for u in node.users))
+        and (
+            dst.dtype == torch.float32
+            or config.EXTENSIONS
+            or not any(_is_fusible(u) for u in node.users)
+        )
     )
 
 
@@ -139,7 +146,7 @@ def build_fused_op(group: list[fx.Node], inputs: list[fx.Node]):
     ``torch.ops.b200.pointwise(inputs, code, imm, out_shape, out_dtype)``.
     Raises ProgramError when the group does not fit the kernel."""
     out_meta = _tensor_meta(group[-1])
-    prog = compile_group(group, inputs)
+    prog = compile_group(group, inputs, rounding_casts=config.EXTENSIONS)
     shape, dtype = [int(s) for s in out_meta.shape], out_meta.dtype
     return prog, shape, dtype
 

@@ -99,6 +99,41 @@ def round_op_for(dtype: torch.dtype) -> str | None:
     return None
 
 
+def _schedule(group: list[fx.Node]) -> list[fx.Node]:
+    """Re-order a group for few live values: depth-first from the output,
+    evaluating the operand with the larger subtree first (Sethi-Ullman
+    order), so each value is produced right before it is consumed.  Every op
+    is a pure elementwise function, so the order does not change any value."""
+    members = set(group)
+    size: dict[fx.Node, int] = {}
+
+    def subtree(n: fx.Node) -> int:
+        if n in size:
+            return size[n]
+        size[n] = 1 + sum(subtree(a) for a in n.args if isinstance(a, fx.Node) and a in members)
+        return size[n]
+
+    order: list[fx.Node] = []
+    seen: set[fx.Node] = set()
+    stack: list[tuple[fx.Node, bool]] = [(group[-1], False)]
+    while stack:
+        n, expanded = stack.pop()
+        if n in seen:
+            continue
+        if expanded:
+            seen.add(n)
+            order.append(n)
+            continue
+        stack.append((n, True))
+        kids = [a for a in n.args if isinstance(a, fx.Node) and a in members and a not in seen]
+        # pushed last = visited first: the biggest subtree goes first
+        for a in sorted(kids, key=subtree):
+            stack.append((a, False))
+    # Members that do not feed the output (impossible for the single-output
+    # groups the passes build) are dropped: they cannot change the result.
+    return order
+
+
 def compile_group(
     group: list[fx.Node],
     operands: list[fx.Node],
@@ -116,7 +151,7 @@ def compile_group(
     are identities as in the reference.
     """
     prog = Program()
-    members = set(group)
+    group = _schedule(group)  # ends with the original output node
 
     # Casts alias their input unless they round.
     alias: dict[fx.Node, fx.Node] = {}
