@@ -340,6 +340,63 @@ def run_sweep(args, dist: Dist) -> dict:
     }
 
 
+def run_single_gemm(args, dist: Dist) -> dict:
+    """One sweep point on its own: --shape M,N,K --act none|gelu|silu [--tile-config c].
+    Used for ncu captures and for measuring the tile table."""
+    from bench_models import GemmEpilogueBlock, init_sweep_block
+    from compiler import runtime
+
+    runtime.load()
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    M, N, K = (int(v) for v in args.shape.split(","))
+    gen = torch.Generator(device=dev).manual_seed(0)
+    x = (0.02 * torch.randn(M, K, device=dev, generator=gen)).to(torch.bfloat16)
+    r = (0.02 * torch.randn(M, N, device=dev, generator=gen)).to(torch.bfloat16)
+    blk = GemmEpilogueBlock(K, N, args.act)
+    init_sweep_block(blk, torch.Generator().manual_seed(0))
+    blk = blk.to(dev, torch.bfloat16).eval()
+    code, imm = _pass_program(blk, x, r)
+    w, b = blk.lin.weight, blk.lin.bias
+    if args.tile_config >= 0:
+        from compiler.runtime import cabi
+
+        out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+
+        def call():
+            cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=args.tile_config)
+            return out
+    else:
+        def call():
+            return torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], code, imm, [M, N], torch.bfloat16)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        call()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    # host cost per call: back-to-back calls, one sync at the end
+    t0 = time.perf_counter()
+    for _ in range(50):
+        call()
+    torch.cuda.synchronize()
+    wall_us = (time.perf_counter() - t0) / 50 * 1e6
+    ms = statistics.median(times)
+    return {"metric": "fused GEMM+epilogue TFLOP/s", "value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "gemm_epilogue", "M": M, "N": N, "K": K, "act": args.act,
+                       "tile_config": args.tile_config, "program_len": len(code)},
+            "back_to_back_us_per_call": round(wall_us, 1)}
+
+
 # --------------------------------------------------------------- CPU (oracle) leg
 def cpu_sweep(rows: int, reps: int) -> dict:
     """The oracle's GEMM + epilogue (numpy fp32, every host core via BLAS) on
@@ -380,7 +437,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sweep", choices=["sweep"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm"])
+    ap.add_argument("--shape", default="4096,4096,4096", help="M,N,K for --workload gemm")
+    ap.add_argument("--act", default="gelu", choices=ACTS, help="epilogue activation for --workload gemm")
+    ap.add_argument("--tile-config", type=int, default=-1, help="force a GEMM tile config (gemm workload)")
     ap.add_argument("--cpu-rows", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
@@ -403,6 +463,9 @@ def main() -> None:
 
     dist = Dist()
     try:
+        if args.workload == "gemm":
+            print(json.dumps(run_single_gemm(args, dist)))
+            return
         res = run_sweep(args, dist)
         if dist.rank == 0:
             if dist.world == 1:

@@ -49,6 +49,7 @@ def test_host_side_errors_need_no_gpu():
     a.n_inputs = 0
     assert lib.b200k_pointwise(ctypes.byref(a), None) == 1
     g = cabi.GemmArgs()
+    g.M, g.N, g.K = 4, 4, 8
     assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 1  # null pointers
     g.a = g.b = g.out = 16
     g.M, g.N, g.K = 4, 4, 0
@@ -61,7 +62,10 @@ def test_host_side_errors_need_no_gpu():
     g.program = cabi.make_program([999], [0.0])
     assert lib.b200k_gemm_epilogue(ctypes.byref(g), None) == 7  # malformed program
     r = cabi.RowNormArgs()
-    assert lib.b200k_rownorm(ctypes.byref(r), None) == 1
+    r.rows, r.cols = 4, 8
+    assert lib.b200k_rownorm(ctypes.byref(r), None) == 1  # null x / out
+    r.rows = 0
+    assert lib.b200k_rownorm(ctypes.byref(r), None) == 0  # empty: nothing to do
 
 
 STRUCTS = {

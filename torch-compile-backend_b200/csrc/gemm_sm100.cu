@@ -635,9 +635,10 @@ extern "C" int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K) {
 }
 
 extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
-  if (!a || !a->a || !a->b || !a->out) return B200K_ERR_ARG;
+  if (!a) return B200K_ERR_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200K_ERR_SHAPE;
-  if (a->M == 0 || a->N == 0) return B200K_OK;
+  if (a->M == 0 || a->N == 0) return B200K_OK;  // empty output: nothing to launch
+  if (!a->a || !a->b || !a->out) return B200K_ERR_ARG;
   if (a->K == 0) return B200K_ERR_SHAPE;
   if (a->M > 0x7fffffff || a->N > 0x7fffffff || a->K > 0x7fffffff) return B200K_ERR_SHAPE;
   if (a->ab_dtype != B200K_BF16 && a->ab_dtype != B200K_F16) return B200K_ERR_UNSUPPORTED;

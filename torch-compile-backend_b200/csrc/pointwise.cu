@@ -141,22 +141,22 @@ extern "C" int b200k_pointwise(const B200kPointwiseArgs* a, void* stream_) {
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   if (a->rank < 0 || a->rank > B200K_MAX_DIMS) return B200K_ERR_SHAPE;
   if (a->n_inputs < 1 || a->n_inputs > B200K_MAX_INPUTS) return B200K_ERR_ARG;
-  if (!a->out) return B200K_ERR_ARG;
   if (!valid_float_dtype(a->out_dtype)) return B200K_ERR_UNSUPPORTED;
   int rc = validate_program(a->program, a->n_inputs);
   if (rc != B200K_OK) return rc;
-  for (int i = 0; i < a->n_inputs; ++i) {
-    if (!a->inputs[i].ptr) return B200K_ERR_ARG;
+  for (int i = 0; i < a->n_inputs; ++i)
     if (!valid_dtype(a->inputs[i].dtype)) return B200K_ERR_UNSUPPORTED;
-  }
-
-  // Collect non-trivial dims (outermost first); output is contiguous.
   int64_t numel = 1;
   for (int d = 0; d < a->rank; ++d) {
     if (a->sizes[d] < 0) return B200K_ERR_SHAPE;
     numel *= a->sizes[d];
   }
-  if (numel == 0) return B200K_OK;
+  if (numel == 0) return B200K_OK;  // empty tensors may carry null pointers
+  if (!a->out) return B200K_ERR_ARG;
+  for (int i = 0; i < a->n_inputs; ++i)
+    if (!a->inputs[i].ptr) return B200K_ERR_ARG;
+
+  // Collect non-trivial dims (outermost first); output is contiguous.
   const int nin = a->n_inputs;
   Dim dims[B200K_MAX_DIMS];
   int nd = 0;

@@ -345,8 +345,9 @@ bool row_vec_ok(const void* ptr, int64_t stride, int64_t len) {
 using namespace b200k;
 
 extern "C" int b200k_rownorm(const B200kRowNormArgs* a, void* stream_) {
-  if (!a || !a->x || !a->out) return B200K_ERR_ARG;
+  if (!a) return B200K_ERR_ARG;
   if (a->rows < 0 || a->cols <= 0) return B200K_ERR_SHAPE;
+  if (a->rows > 0 && (!a->x || !a->out)) return B200K_ERR_ARG;
   if (a->kind < B200K_ROW_RMSNORM || a->kind > B200K_ROW_RMSNORM_SWIGLU) return B200K_ERR_ARG;
   const bool swiglu = a->kind == B200K_ROW_RMSNORM_SWIGLU;
   const bool layer = a->kind == B200K_ROW_LAYERNORM;
@@ -391,8 +392,9 @@ extern "C" int b200k_rownorm(const B200kRowNormArgs* a, void* stream_) {
 }
 
 extern "C" int b200k_softmax(const B200kSoftmaxArgs* a, void* stream_) {
-  if (!a || !a->x || !a->out) return B200K_ERR_ARG;
+  if (!a) return B200K_ERR_ARG;
   if (a->rows < 0 || a->cols <= 0) return B200K_ERR_SHAPE;
+  if (a->rows > 0 && (!a->x || !a->out)) return B200K_ERR_ARG;
   for (int dt : {a->x_dtype, a->out_dtype})
     if (dt != B200K_F32 && dt != B200K_F16 && dt != B200K_BF16) return B200K_ERR_UNSUPPORTED;
   if (a->rows == 0) return B200K_OK;
