@@ -196,7 +196,8 @@ def _pass_program(block, x, r):
         torch.compile(block, backend=be)(x[:128], r[:128])
     if len(found) != 1:
         raise RuntimeError(f"expected one fused GEMM+epilogue node, got {len(found)}")
-    return list(found[0].args[3]), list(found[0].args[4])
+    n = found[0]
+    return list(n.args[3]), list(n.args[4]), list(n.args[7]) if len(n.args) > 7 else []
 
 
 def _smi_id(local: int) -> str:
@@ -223,10 +224,11 @@ def run_sweep(args, dist: Dist) -> dict:
     outs = []
     for p in probs:
         M, N, K = p["shape"]
-        code, imm = _pass_program(p["block"], p["x"], p["r"])
+        code, imm, form = _pass_program(p["block"], p["x"], p["r"])
+        p["form"] = form
         lin = p["block"].lin
-        p["call"] = (lambda x=p["x"], w=lin.weight, b=lin.bias, r=p["r"], c=code, i=imm, s=[M, N]:
-                     torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], c, i, s, torch.bfloat16))
+        p["call"] = (lambda x=p["x"], w=lin.weight, b=lin.bias, r=p["r"], c=code, i=imm, s=[M, N], f=form:
+                     torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], c, i, s, torch.bfloat16, f))
     flops = sum(2.0 * p["shape"][0] * p["shape"][1] * p["shape"][2] for p in probs)
 
     def step(record=None):
@@ -336,6 +338,7 @@ def run_sweep(args, dist: Dist) -> dict:
         "gpu_launches": args.steps * len(probs),
         "clocks": clk.summary(),
         "sweep": sweep_detail,
+        "epilogue_paths": sorted({"compiled" if p["form"] else "interpreted" for p in probs}),
         "spot_check_max_rel_err": round(err, 5),
     }
 
@@ -356,7 +359,9 @@ def run_single_gemm(args, dist: Dist) -> dict:
     blk = GemmEpilogueBlock(K, N, args.act)
     init_sweep_block(blk, torch.Generator().manual_seed(0))
     blk = blk.to(dev, torch.bfloat16).eval()
-    code, imm = _pass_program(blk, x, r)
+    code, imm, form = _pass_program(blk, x, r)
+    if args.interpret:
+        form = []
     w, b = blk.lin.weight, blk.lin.bias
     if args.tile_config >= 0:
         from compiler.runtime import cabi
@@ -364,11 +369,11 @@ def run_single_gemm(args, dist: Dist) -> dict:
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
 
         def call():
-            cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=args.tile_config)
+            cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=args.tile_config, form=form)
             return out
     else:
         def call():
-            return torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], code, imm, [M, N], torch.bfloat16)
+            return torch.ops.b200.gemm_epilogue(x, w.t(), [b, r], code, imm, [M, N], torch.bfloat16, form)
     flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
     for _ in range(args.warmup):
         call()
@@ -393,7 +398,8 @@ def run_single_gemm(args, dist: Dist) -> dict:
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "gemm_epilogue", "M": M, "N": N, "K": K, "act": args.act,
-                       "tile_config": args.tile_config, "program_len": len(code)},
+                       "tile_config": args.tile_config, "program_len": len(code),
+                       "epilogue_path": "compiled" if form else "interpreted"},
             "back_to_back_us_per_call": round(wall_us, 1)}
 
 
@@ -441,6 +447,7 @@ def main() -> None:
     ap.add_argument("--shape", default="4096,4096,4096", help="M,N,K for --workload gemm")
     ap.add_argument("--act", default="gelu", choices=ACTS, help="epilogue activation for --workload gemm")
     ap.add_argument("--tile-config", type=int, default=-1, help="force a GEMM tile config (gemm workload)")
+    ap.add_argument("--interpret", action="store_true", help="gemm workload: interpret the epilogue program")
     ap.add_argument("--cpu-rows", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

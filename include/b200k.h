@@ -154,6 +154,34 @@ typedef struct {
 } B200kEpiOperand;
 
 /*
+ * Canonical epilogue form.  When a program computes
+ *     v = acc;  v += E[bias];  v = act(v);  v = round(v);  v *= E[scale];  v += E[residual]
+ * (each step optional; E[i] = extras[i]) the GEMM kernel runs a compiled
+ * path instead of interpreting the program.  The library checks the form
+ * against the program (host-side evaluation on probe values) and rejects a
+ * mismatch with B200K_ERR_PROGRAM.  kind = 0 always interprets.
+ */
+enum {
+  B200K_ACT_NONE = 0,
+  B200K_ACT_GELU_ERF = 1,   /* x*0.5 * (1 + erf(x*0.70710678)) */
+  B200K_ACT_GELU_TANH = 2,  /* x*0.5 * (1 + tanh(0.79788456*(x + 0.044715*x^3))) */
+  B200K_ACT_SILU = 3,       /* x * sigmoid(x) */
+  B200K_ACT_RELU = 4,
+  B200K_ACT_SIGMOID = 5,
+  B200K_ACT_TANH = 6,
+  B200K_ACT_COUNT = 7
+};
+
+typedef struct {
+  int32_t kind;     /* 0 = interpret the program, 1 = canonical form */
+  int32_t bias;     /* extras index or -1 */
+  int32_t act;      /* B200K_ACT_* */
+  int32_t round;    /* -1 none, else B200K_BF16 / B200K_F16: round after act */
+  int32_t scale;    /* extras index or -1 */
+  int32_t residual; /* extras index or -1 */
+} B200kEpilogueForm;
+
+/*
  * out[m,n] = program(acc[m,n], extras[..][m,n]) with acc = sum_k a[m,k]*b[k,n]
  * accumulated in fp32 on the tcgen05 tensor cores.  a is [M,K] with unit K
  * stride; b is the reference's mat2 [K,N] (usually t(W) with unit K stride,
@@ -178,6 +206,8 @@ typedef struct {
   B200kProgram program;
   int32_t* status;     /* optional device word: set to B200K_ERR_TIMEOUT by a stuck wait */
   int64_t timeout_ns;  /* 0 = default (2 s) */
+  B200kEpilogueForm form;
+  int32_t pad2;
 } B200kGemmArgs;
 
 int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);

@@ -15,7 +15,7 @@ import torch
 import oracle
 import spec_graph
 from compiler import runtime
-from compiler.optimization.program import OP, compile_group
+from compiler.optimization.program import OP, canonical_form, compile_group
 from compiler.runtime import cabi
 
 pytestmark = pytest.mark.gpu
@@ -60,10 +60,10 @@ def epilogue_program(act: str, residual: bool, bias: bool = True):
     nodes, ops = spec_graph.build(spec, n_in, with_acc=True) if spec else (None, None)
     if spec:
         pro = [("ADD", ops[1])] if bias else None
-        prog = compile_group(nodes, ops, prologue=pro, prologue_target=ops[0])
-        return prog.code, prog.imm, spec
+        prog = compile_group(nodes, ops, prologue=pro, prologue_target=ops[0], rounding_casts=True)
+        return prog.code, prog.imm, spec, canonical_form(prog, 1 + n_in)
     # bias only: acc + bias
-    return [OP["MOV"] * 10, OP["ADD"] * 10 + 1], [0.0, 0.0], []
+    return [OP["MOV"] * 10, OP["ADD"] * 10 + 1], [0.0, 0.0], [], [1, 0, 0, -1, -1, -1]
 
 
 @pytest.fixture(scope="module", autouse=True)
@@ -116,19 +116,22 @@ SWEEP = [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 
 
 @pytest.mark.parametrize("shape", SWEEP)
 @pytest.mark.parametrize("act", ["none", "gelu", "silu"])
-def test_gemm_sweep_configs(shape, act):
-    """The fused GEMM sweep at its full sizes, Y = act(X W^T + b) + R in bf16;
-    checked on 192 sampled rows against the fp32 oracle."""
+@pytest.mark.parametrize("path", ["compiled", "interpreted"])
+def test_gemm_sweep_configs(shape, act, path):
+    """The fused GEMM sweep at its full sizes, Y = act(X W^T + b) + R in bf16,
+    through the compiled epilogue path and the program interpreter; checked
+    on 192 sampled rows against the fp32 oracle."""
     M, N, K = shape
     g = torch.Generator(device=DEV).manual_seed(0)
     x = (0.02 * torch.randn(M, K, device=DEV, generator=g)).to(torch.bfloat16)
     w = (0.02 * torch.randn(N, K, device=DEV, generator=g)).to(torch.bfloat16)
     b = (0.01 * torch.randn(N, device=DEV, generator=g)).to(torch.bfloat16)
     r = (0.02 * torch.randn(M, N, device=DEV, generator=g)).to(torch.bfloat16)
-    code, imm, spec = epilogue_program(act, residual=True)
+    code, imm, spec, form = epilogue_program(act, residual=True)
+    assert form is not None
     out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, status=status)
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, status=status, form=form if path == "compiled" else None)
     torch.cuda.synchronize()
     assert status.item() == 0
     rows = torch.randperm(M, generator=torch.Generator().manual_seed(1))[:192].sort().values
@@ -144,7 +147,8 @@ def test_gemm_sweep_configs(shape, act):
                                    (257, 1000, 768), (64, 4096, 1024)])
 @pytest.mark.parametrize("config", [0, 1])
 @pytest.mark.parametrize("ab", ["bfloat16", "float16"])
-def test_gemm_edge_shapes(M, N, K, config, ab):
+@pytest.mark.parametrize("path", ["compiled", "interpreted"])
+def test_gemm_edge_shapes(M, N, K, config, ab, path):
     """Ragged M/N/K (partial tiles, K tail inside a 64-wide block, M < 128,
     N whose rows are not 16-byte multiples -> direct-store path), both tile
     configs, both operand dtypes, gelu-tanh + bias + residual."""
@@ -154,9 +158,11 @@ def test_gemm_edge_shapes(M, N, K, config, ab):
     w = torch.randn(N, K, device=DEV, generator=g).to(dt)
     b = torch.randn(N, device=DEV, generator=g).to(dt)
     r = torch.randn(M, N, device=DEV, generator=g).to(dt)
-    code, imm, spec = epilogue_program("gelu_tanh", residual=True)
+    code, imm, spec, form = epilogue_program("gelu_tanh", residual=True)
+    assert form is not None
     out = torch.empty(M, N, device=DEV, dtype=dt)
-    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=config)
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=config,
+                       form=form if path == "compiled" else None)
     torch.cuda.synchronize()
     want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
                                 [b.float().cpu().numpy(), r.float().cpu().numpy()], ab, bias=b.float().cpu().numpy())
@@ -329,3 +335,16 @@ def test_softmax(rows, cols, log):
     if not log:  # every row sums to one
         s = out.float().sum(-1)
         assert torch.allclose(s, torch.ones_like(s), atol=2e-2)
+
+
+def test_gemm_rejects_form_that_contradicts_program():
+    x = torch.randn(64, 64, device=DEV).to(torch.bfloat16)
+    w = torch.randn(64, 64, device=DEV).to(torch.bfloat16)
+    b = torch.randn(64, device=DEV).to(torch.bfloat16)
+    code, imm, spec, form = epilogue_program("gelu", residual=False)
+    out = torch.empty(64, 64, device=DEV, dtype=torch.bfloat16)
+    bad = list(form)
+    bad[2] = 3  # claims SiLU
+    with pytest.raises(cabi.CError) as e:
+        cabi.gemm_epilogue(x, w.t(), [b], code, imm, out, form=bad)
+    assert e.value.code == 7

@@ -235,3 +235,55 @@ def test_fp32_gemm_left_to_aten():
     (gm,) = fused_graphs(model, inputs)
     t = _targets(gm)
     assert aten.addmm.default in t and torch.ops.b200.pointwise.default in t
+
+
+def _epi_nodes(model, inputs):
+    from helpers import fused_graphs as fg
+    (gm,) = fg(model, inputs)
+    return [n for n in gm.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.gemm_epilogue.default]
+
+
+@pytest.mark.parametrize("act,code", [("none", 0), ("gelu", 1), ("silu", 3)])
+def test_sweep_epilogues_take_the_compiled_path(act, code):
+    import bench_models as bm
+    m = bm.GemmEpilogueBlock(64, 128, act).to(torch.bfloat16)
+    (n,) = _epi_nodes(m, (torch.randn(32, 64).to(torch.bfloat16), torch.randn(32, 128).to(torch.bfloat16)))
+    rnd = -1 if act == "none" else 2  # bf16 rounding after the activation
+    assert list(n.args[7]) == [1, 0, code, rnd, -1, 1]
+
+
+def test_canonical_form_variants():
+    """MLPBlock fc2 (x + tanh(y)*scale), tanh-GELU, and a non-canonical chain."""
+    model, inputs = make_case("mlp_block_fp16")
+    forms = [list(n.args[7]) for n in _epi_nodes(model, inputs)]
+    assert [1, 0, 6, -1, 1, 2] in forms        # bias, tanh, *scale, +x
+    assert [1, 0, 1, -1, -1, -1] in forms       # bias, gelu(erf)
+    model, inputs = make_case("mlp_tanh_fp16")
+    forms = [list(n.args[7]) for n in _epi_nodes(model, inputs)]
+    assert [1, 0, 2, -1, -1, -1] in forms and [1, 0, 0, -1, -1, 1] in forms
+
+    class Odd(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = nn.Linear(64, 64)
+
+        def forward(self, x):
+            return torch.exp(self.fc(x)) * x - 1.0
+
+    (n,) = _epi_nodes(Odd().half(), (torch.randn(16, 64).half(),))
+    assert list(n.args[7]) == []  # interpreted
+
+
+def test_llama_gate_up_epilogue_is_canonical():
+    """silu(gate(h)) * up(h): the gate GEMM's epilogue multiplies by the up GEMM output."""
+    class SwiGLU(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.g = nn.Linear(64, 128, bias=False)
+            self.u = nn.Linear(64, 128, bias=False)
+
+        def forward(self, h):
+            return F.silu(self.g(h)) * self.u(h)
+
+    forms = [list(n.args[7]) for n in _epi_nodes(SwiGLU().to(torch.bfloat16), (torch.randn(2, 8, 64).to(torch.bfloat16),))]
+    assert [1, -1, 3, 2, 0, -1] in forms

@@ -7,6 +7,7 @@ Environment flags (read once at import, overridable as module attributes):
   B200_POINTWISE=0    skip the pointwise pass
   B200_ROWREDUCE=0    skip the row-reduction pass
   B200_DUMP=1         print each compiled graph and the fused-kernel programs
+  B200_FAST_EPILOGUE=0  always interpret GEMM epilogue programs
 
 The reference hard-codes its equivalents (AUTOTUNE_CONFIGS, BLOCK=1024,
 DOT_DTYPES in compiler/optimization/fusion_epilogue.py:23-38 and
@@ -30,6 +31,7 @@ ENABLE_EPILOGUE = _flag("B200_EPILOGUE", True)
 ENABLE_POINTWISE = _flag("B200_POINTWISE", True)
 ENABLE_ROWREDUCE = _flag("B200_ROWREDUCE", True)
 DUMP = _flag("B200_DUMP", False)
+FAST_EPILOGUE = _flag("B200_FAST_EPILOGUE", True)  # compiled path for canonical GEMM epilogues
 
 # Kernel library limits (include/b200k.h).
 MAX_INPUTS = 8

@@ -29,7 +29,7 @@ from compiler import runtime
 
 from . import config
 from .fusion_pointwise import _tensor_meta, external_inputs, find_fusion_groups, new_kernel_name
-from .program import ProgramError, compile_group
+from .program import ProgramError, canonical_form, compile_group
 
 aten = torch.ops.aten
 runtime.load()
@@ -159,6 +159,12 @@ def build_epilogue_op(group, matmul, inputs, anchor=None):
     return prog, [int(s) for s in out_meta.shape], out_meta.dtype
 
 
+def epilogue_form(prog, n_operands: int) -> list[int]:
+    """The kernel's compiled-path descriptor for this program ([] = interpret)."""
+    form = canonical_form(prog, n_operands) if config.FAST_EPILOGUE else None
+    return form or []
+
+
 def _epilogue_is_faster(group, matmul, inputs) -> bool:
     """Profitability rule standing in for the reference's compile-time
     wall-clock race (:207-234).  The fused kernel does the same tensor-core
@@ -189,7 +195,7 @@ def fuse_epilogue(gm: fx.GraphModule) -> fx.GraphModule:
         with gm.graph.inserting_before(root):
             new_node = gm.graph.call_function(
                 torch.ops.b200.gemm_epilogue.default,
-                (mat1, mat2, list(inputs), prog.code, prog.imm, shape, dtype),
+                (mat1, mat2, list(inputs), prog.code, prog.imm, shape, dtype, epilogue_form(prog, 1 + len(inputs))),
             )
         new_node.meta = dict(root.meta)
         new_node.meta["b200_kernel"] = new_kernel_name("gemm_epilogue")

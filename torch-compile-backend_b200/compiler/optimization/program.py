@@ -304,3 +304,97 @@ def group_spec(group: list[fx.Node], operands: list[fx.Node]) -> list[tuple]:
             args.append(str(node.kwargs.get("dtype")).replace("torch.", ""))
         spec.append((name, tuple(args)))
     return spec
+
+
+# ------------------------------------------------------------------ canonical form
+# The GEMM kernel has a compiled path for programs of the form
+#   v = acc [+ E_bias]; v = act(v); [v = round(v)]; [v *= E_scale]; [v += E_res]
+# (include/b200k.h, B200kEpilogueForm).  canonical_form() recognises it by
+# executing the program symbolically and comparing expression trees, with
+# commutative operands in a fixed order.
+ACT_CODES = {"NONE": 0, "GELU_ERF": 1, "GELU_TANH": 2, "SILU": 3, "RELU": 4, "SIGMOID": 5, "TANH": 6}
+_DT_BF16, _DT_F16 = 2, 1
+
+
+def _f32(v: float) -> float:
+    import struct
+
+    return struct.unpack("f", struct.pack("f", float(v)))[0]
+
+
+def _mk(name: str, a, b):
+    if name in ("add", "mul", "max", "min"):
+        return (name,) + tuple(sorted((a, b), key=repr))
+    return (name, a, b)
+
+
+def _const(v):
+    return ("c", _f32(v))
+
+
+_ACT_TEMPLATES = {
+    "NONE": lambda x: x,
+    "GELU_ERF": lambda x: _mk("mul", _mk("mul", x, _const(0.5)),
+                              _mk("add", ("erf", _mk("mul", x, _const(0.7071067811865476))), _const(1.0))),
+    "GELU_TANH": lambda x: _mk("mul", _mk("mul", x, _const(0.5)), _mk("add", ("tanh", _mk(
+        "mul", _mk("add", x, _mk("mul", _mk("mul", _mk("mul", x, x), x), _const(0.044715))),
+        _const(0.7978845608028654))), _const(1.0))),
+    "SILU": lambda x: _mk("mul", x, ("sigmoid", x)),
+    "RELU": lambda x: ("relu", x),
+    "SIGMOID": lambda x: ("sigmoid", x),
+    "TANH": lambda x: ("tanh", x),
+}
+
+_SYM_BIN = {"ADD": "add", "SUB": "sub", "MUL": "mul", "DIV": "div", "MAX": "max", "MIN": "min"}
+
+
+def symbolic(code: list[int], imm: list[float], n_operands: int):
+    """Expression tree the program leaves in the accumulator."""
+    slots = [("in", i) for i in range(n_operands)] + [("zero",)] * (MAX_SLOTS - n_operands)
+    acc = slots[0]
+    for c, v in zip(code, imm):
+        op, o = divmod(int(c), 10)
+        name = OP_NAME[op]
+        x = slots[o] if o < MAX_SLOTS else (_const(v) if o == OPERAND_IMM else None)
+        if name == "MOV":
+            acc = x
+        elif name == "STORE":
+            slots[o] = acc
+        elif name in _SYM_BIN:
+            acc = _mk(_SYM_BIN[name], acc, x)
+        elif name == "RSUB":
+            acc = _mk("sub", x, acc)
+        elif name == "RDIV":
+            acc = _mk("div", x, acc)
+        elif name != "NOP":
+            acc = (name.lower(), acc)
+    return acc
+
+
+def canonical_form(prog: Program, n_operands: int) -> list[int] | None:
+    """[1, bias, act, round, scale, residual] (extras indices, -1 = absent) when
+    the GEMM-epilogue program (slot 0 = accumulator) has the canonical form."""
+    tree = symbolic(prog.code, prog.imm, n_operands)
+
+    def peel(t, op):
+        yield t, -1
+        if t[0] == op:
+            for inner, leaf in ((t[1], t[2]), (t[2], t[1])):
+                if leaf[0] == "in" and 1 <= leaf[1] < n_operands:
+                    yield inner, leaf[1]
+
+    for t1, res in peel(tree, "add"):
+        for t2, scale in peel(t1, "mul"):
+            rounds = [(t2, -1)]
+            if t2[0] == "round_bf16":
+                rounds.append((t2[1], _DT_BF16))
+            if t2[0] == "round_f16":
+                rounds.append((t2[1], _DT_F16))
+            for t3, rnd in rounds:
+                for act, tmpl in _ACT_TEMPLATES.items():
+                    for bias in [-1] + list(range(1, n_operands)):
+                        base = ("in", 0) if bias < 0 else _mk("add", ("in", 0), ("in", bias))
+                        if tmpl(base) == t3:
+                            return [1, bias - 1 if bias > 0 else -1, ACT_CODES[act], rnd,
+                                    scale - 1 if scale > 0 else -1, res - 1 if res > 0 else -1]
+    return None

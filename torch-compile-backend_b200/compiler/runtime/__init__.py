@@ -45,7 +45,7 @@ def _register_fakes() -> None:
         return inputs[0].new_empty(out_shape, dtype=out_dtype)
 
     @torch.library.register_fake(lib + "gemm_epilogue")
-    def _(a, b, extras, code, imm, out_shape, out_dtype):
+    def _(a, b, extras, code, imm, out_shape, out_dtype, form=()):
         return a.new_empty(out_shape, dtype=out_dtype)
 
     @torch.library.register_fake(lib + "rms_norm")

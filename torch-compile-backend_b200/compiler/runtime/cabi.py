@@ -55,6 +55,11 @@ class EpiOperand(ctypes.Structure):
                 ("stride_m", ctypes.c_int64), ("stride_n", ctypes.c_int64)]
 
 
+class EpilogueForm(ctypes.Structure):
+    _fields_ = [("kind", ctypes.c_int32), ("bias", ctypes.c_int32), ("act", ctypes.c_int32),
+                ("round", ctypes.c_int32), ("scale", ctypes.c_int32), ("residual", ctypes.c_int32)]
+
+
 class GemmArgs(ctypes.Structure):
     _fields_ = [("M", ctypes.c_int64), ("N", ctypes.c_int64), ("K", ctypes.c_int64),
                 ("a", ctypes.c_void_p), ("a_stride_m", ctypes.c_int64), ("a_stride_k", ctypes.c_int64),
@@ -63,7 +68,8 @@ class GemmArgs(ctypes.Structure):
                 ("out", ctypes.c_void_p), ("out_stride_m", ctypes.c_int64), ("out_stride_n", ctypes.c_int64),
                 ("n_extras", ctypes.c_int32), ("tile_config", ctypes.c_int32),
                 ("extras", EpiOperand * (MAX_INPUTS - 1)), ("program", Program),
-                ("status", ctypes.c_void_p), ("timeout_ns", ctypes.c_int64)]
+                ("status", ctypes.c_void_p), ("timeout_ns", ctypes.c_int64), ("form", EpilogueForm),
+                ("pad2", ctypes.c_int32)]
 
 
 class RowNormArgs(ctypes.Structure):
@@ -156,7 +162,8 @@ def pointwise(inputs: list[torch.Tensor], code, imm, out: torch.Tensor) -> None:
 
 
 def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], code, imm, out: torch.Tensor,
-                  tile_config: int = -1, status: torch.Tensor | None = None, timeout_ns: int = 0) -> None:
+                  tile_config: int = -1, status: torch.Tensor | None = None, timeout_ns: int = 0,
+                  form=None) -> None:
     """out[M,N] = program(a @ b, extras) with extras given as [M,N]-broadcastable tensors."""
     g = GemmArgs()
     M, K = a.shape
@@ -178,6 +185,8 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
     g.program = make_program(code, imm)
     g.status = status.data_ptr() if status is not None else None
     g.timeout_ns = timeout_ns
+    if form:
+        (g.form.kind, g.form.bias, g.form.act, g.form.round, g.form.scale, g.form.residual) = form
     _check("b200k_gemm_epilogue", library().b200k_gemm_epilogue(ctypes.byref(g), _stream()))
 
 

@@ -71,7 +71,7 @@ struct Params {
   int32_t* status;
   int64_t timeout_ns;
   uint32_t idesc;
-  int32_t pad;
+  int32_t f_bias, f_act, f_round, f_scale, f_res;  // canonical epilogue form (fast path)
   EpiOperand ex[B200K_MAX_INPUTS - 1];
   B200kProgram prog;
 };
@@ -204,6 +204,23 @@ __device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int
   tn = r / gsize;
 }
 
+// Epilogue operand values at (m, n..n+7), zero outside [M, N).
+__device__ __forceinline__ void load_extra8(const EpiOperand& e, int m, int n, int M, int N, float (&v)[8]) {
+  if (m < M && n + 8 <= N && e.vec) {
+    load_vec8(e.ptr, static_cast<int64_t>(m) * e.sm + n, e.dt, v);
+  } else if (e.sn == 0) {
+    const float s = (m < M) ? load_scalar(e.ptr, static_cast<int64_t>(m) * e.sm, e.dt) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = s;
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      v[j] = (m < M && n + j < N)
+                 ? load_scalar(e.ptr, static_cast<int64_t>(m) * e.sm + static_cast<int64_t>(n + j) * e.sn, e.dt)
+                 : 0.0f;
+  }
+}
+
 // Epilogue operand values at (m, n..n+3), zero outside [M, N).
 __device__ __forceinline__ void load_extra4(const EpiOperand& e, int m, int n, int M, int N, float (&v)[4]) {
   if (m < M && n + 4 <= N && e.vec) {
@@ -234,6 +251,13 @@ __device__ __forceinline__ void load_extra4(const EpiOperand& e, int m, int n, i
                  ? load_scalar(e.ptr, static_cast<int64_t>(m) * e.sm + static_cast<int64_t>(n + j) * e.sn, e.dt)
                  : 0.0f;
   }
+}
+
+// 32 lanes x 32 bit, 8 consecutive columns.
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
 }
 
 // 32 lanes x 32 bit, 4 consecutive columns.
@@ -300,6 +324,107 @@ __device__ __forceinline__ void epilogue_group(const Params& p, uint32_t taddr, 
   }
 }
 
+// ------------------------------------------------------- canonical fast path
+// v = acc; v += E[bias]; v = act(v); v = round(v); v *= E[scale]; v += E[res]
+// with the same fp32 operation order as the decomposed ATen graph it replaces.
+__device__ __forceinline__ void apply_act8(int act, float (&v)[8]) {
+  switch (act) {
+    case B200K_ACT_GELU_ERF:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float t0 = v[j] * 0.5f;
+        const float t1 = erff(v[j] * 0.7071067811865476f) + 1.0f;
+        v[j] = t0 * t1;
+      }
+      break;
+    case B200K_ACT_GELU_TANH:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float x = v[j];
+        const float t3 = x + ((x * x) * x) * 0.044715f;
+        const float t6 = op_tanh(t3 * 0.7978845608028654f) + 1.0f;
+        v[j] = (x * 0.5f) * t6;
+      }
+      break;
+    case B200K_ACT_SILU:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * op_sigmoid(v[j]);
+      break;
+    case B200K_ACT_RELU:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = fmaxf(v[j], 0.0f);
+      break;
+    case B200K_ACT_SIGMOID:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = op_sigmoid(v[j]);
+      break;
+    case B200K_ACT_TANH:
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = op_tanh(v[j]);
+      break;
+    default:
+      break;
+  }
+}
+
+using FastRegs = float[3][8];  // bias, scale, residual for one 8-column group
+
+__device__ __forceinline__ void load_fast(const Params& p, int m, int n, FastRegs& x) {
+  if (p.f_bias >= 0) load_extra8(p.ex[p.f_bias], m, n, p.M, p.N, x[0]);
+  if (p.f_scale >= 0) load_extra8(p.ex[p.f_scale], m, n, p.M, p.N, x[1]);
+  if (p.f_res >= 0) load_extra8(p.ex[p.f_res], m, n, p.M, p.N, x[2]);
+}
+
+template <int OUT_BYTES>
+__device__ __forceinline__ void epilogue_group_fast(const Params& p, uint32_t taddr, int m, int n, int g, int lane,
+                                                    uint8_t* sb, const FastRegs& cur, FastRegs& nxt, bool prefetch) {
+  uint32_t raw[8];
+  tmem_ld8(taddr, raw);
+  if (prefetch) load_fast(p, m, n + 8, nxt);
+  tmem_wait_ld();
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[j]);
+  if (p.f_bias >= 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += cur[0][j];
+  }
+  apply_act8(p.f_act, v);
+  if (p.f_round == B200K_BF16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
+  } else if (p.f_round == B200K_F16) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
+  }
+  if (p.f_scale >= 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] *= cur[1][j];
+  }
+  if (p.f_res >= 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] += cur[2][j];
+  }
+  if (p.direct_store) {
+    if (m < p.M) {
+      const int64_t off = static_cast<int64_t>(m) * p.out_sm + n;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (n + j < p.N) store_scalar(p.out, off + j, p.out_dt, v[j]);
+    }
+  } else if (OUT_BYTES == 2) {
+    const uint4 u = (p.out_dt == B200K_BF16) ? pack_bf16x8(v) : pack_f16x8(v);
+    *reinterpret_cast<uint4*>(sb + lane * 128 + ((g ^ (lane & 7)) << 4)) = u;
+  } else {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int chunk = 2 * g + h;
+      *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    }
+  }
+}
+
 template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
 struct Cfg {
   static constexpr uint32_t kABytes = BM * BK * 2;
@@ -313,7 +438,7 @@ struct Cfg {
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
 };
 
-template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
@@ -474,13 +599,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
         }
-        ExtraRegs xa, xb;
-        load_extras(p, m, n0, xa);
+        if constexpr (FAST) {
+          FastRegs xa, xb;
+          load_fast(p, m, n0, xa);
 #pragma unroll 1
-        for (int g = 0; g < C::kEC / kEV; g += 2) {
-          epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + g * kEV, m, n0 + g * kEV, g, lane, sb, xa, xb, true);
-          epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + (g + 1) * kEV, m, n0 + (g + 1) * kEV, g + 1, lane, sb, xb,
-                                    xa, g + 2 < C::kEC / kEV);
+          for (int g = 0; g < C::kEC / 8; g += 2) {
+            epilogue_group_fast<OUT_BYTES>(p, t_row + c * C::kEC + g * 8, m, n0 + g * 8, g, lane, sb, xa, xb, true);
+            epilogue_group_fast<OUT_BYTES>(p, t_row + c * C::kEC + (g + 1) * 8, m, n0 + (g + 1) * 8, g + 1, lane, sb,
+                                           xb, xa, g + 2 < C::kEC / 8);
+          }
+        } else {
+          ExtraRegs xa, xb;
+          load_extras(p, m, n0, xa);
+#pragma unroll 1
+          for (int g = 0; g < C::kEC / kEV; g += 2) {
+            epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + g * kEV, m, n0 + g * kEV, g, lane, sb, xa, xb, true);
+            epilogue_group<OUT_BYTES>(p, t_row + c * C::kEC + (g + 1) * kEV, m, n0 + (g + 1) * kEV, g + 1, lane, sb,
+                                      xb, xa, g + 2 < C::kEC / kEV);
+          }
         }
         if (!p.direct_store) {
           fence_async_smem();
@@ -558,11 +694,11 @@ struct TileConfig {
 constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-template <int BN, int STAGES, bool BNM, int OB>
+template <int BN, int STAGES, bool BNM, int OB, bool FAST>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
                cudaStream_t st) {
   using C = Cfg<BN, STAGES, BNM, OB>;
-  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB>;
+  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST>;
   static bool attr_set = false;  // per instantiation; idempotent
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
@@ -573,15 +709,22 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
 }
 
-template <int BN, int STAGES>
-int launch_cfg(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-               const Params& p, int grid, cudaStream_t st) {
+template <int BN, int STAGES, bool FAST>
+int launch_cfg_f(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                 const Params& p, int grid, cudaStream_t st) {
   if (bnm) {
-    return ob == 2 ? launch_one<BN, STAGES, true, 2>(ta, tb, to, p, grid, st)
-                   : launch_one<BN, STAGES, true, 4>(ta, tb, to, p, grid, st);
+    return ob == 2 ? launch_one<BN, STAGES, true, 2, FAST>(ta, tb, to, p, grid, st)
+                   : launch_one<BN, STAGES, true, 4, FAST>(ta, tb, to, p, grid, st);
   }
-  return ob == 2 ? launch_one<BN, STAGES, false, 2>(ta, tb, to, p, grid, st)
-                 : launch_one<BN, STAGES, false, 4>(ta, tb, to, p, grid, st);
+  return ob == 2 ? launch_one<BN, STAGES, false, 2, FAST>(ta, tb, to, p, grid, st)
+                 : launch_one<BN, STAGES, false, 4, FAST>(ta, tb, to, p, grid, st);
+}
+
+template <int BN, int STAGES>
+int launch_cfg(bool fast, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+               const Params& p, int grid, cudaStream_t st) {
+  return fast ? launch_cfg_f<BN, STAGES, true>(bnm, ob, ta, tb, to, p, grid, st)
+              : launch_cfg_f<BN, STAGES, false>(bnm, ob, ta, tb, to, p, grid, st);
 }
 
 int pick(int64_t M, int64_t N, int sms) {
@@ -647,6 +790,10 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (a->n_extras < 0 || a->n_extras > B200K_MAX_INPUTS - 1) return B200K_ERR_ARG;
   int rc = validate_program(a->program, 1 + a->n_extras);
   if (rc != B200K_OK) return rc;
+  if (a->form.kind != 0) {
+    rc = check_form(a->form, a->program, a->n_extras);
+    if (rc != B200K_OK) return rc;
+  }
 
   // A: [M, K], unit K stride, rows 16-byte aligned.
   if (a->a_stride_k != 1 && a->K > 1) return B200K_ERR_UNSUPPORTED;
@@ -710,6 +857,11 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
                 : 0;
   }
   p.prog = a->program;
+  p.f_bias = a->form.bias;
+  p.f_act = a->form.act;
+  p.f_round = a->form.round;
+  p.f_scale = a->form.scale;
+  p.f_res = a->form.residual;
 
   CUtensorMap ta, tb, to;
   std::memset(&to, 0, sizeof(to));
@@ -726,6 +878,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   }
   const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  if (cfg == 0) return launch_cfg<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
-  return launch_cfg<128, 6>(bnm, ob, ta, tb, to, p, grid, st);
+  const bool fast = a->form.kind == 1;
+  if (cfg == 0) return launch_cfg<256, 4>(fast, bnm, ob, ta, tb, to, p, grid, st);
+  return launch_cfg<128, 6>(fast, bnm, ob, ta, tb, to, p, grid, st);
 }

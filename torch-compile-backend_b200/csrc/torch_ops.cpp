@@ -119,7 +119,8 @@ void mn_strides(const at::Tensor& t, at::IntArrayRef out_shape, int64_t& sm, int
 }
 
 at::Tensor gemm_epilogue(const at::Tensor& a, const at::Tensor& b, at::TensorList extras, at::IntArrayRef code,
-                         at::ArrayRef<double> imm, at::IntArrayRef out_shape, at::ScalarType out_dtype) {
+                         at::ArrayRef<double> imm, at::IntArrayRef out_shape, at::ScalarType out_dtype,
+                         at::IntArrayRef form) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda(), "b200::gemm_epilogue: a and b must be CUDA tensors");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2, "b200::gemm_epilogue: a [M,K] and b [K,N] must be 2-d");
   TORCH_CHECK(a.size(1) == b.size(0), "b200::gemm_epilogue: incompatible shapes ", a.sizes(), " and ", b.sizes());
@@ -161,6 +162,15 @@ at::Tensor gemm_epilogue(const at::Tensor& a, const at::Tensor& b, at::TensorLis
     g.extras[i].stride_n = sn;
   }
   g.program = make_program(code, imm);
+  TORCH_CHECK(form.empty() || form.size() == 6, "b200::gemm_epilogue: form needs 6 ints");
+  if (form.size() == 6) {
+    g.form.kind = static_cast<int32_t>(form[0]);
+    g.form.bias = static_cast<int32_t>(form[1]);
+    g.form.act = static_cast<int32_t>(form[2]);
+    g.form.round = static_cast<int32_t>(form[3]);
+    g.form.scale = static_cast<int32_t>(form[4]);
+    g.form.residual = static_cast<int32_t>(form[5]);
+  }
   g.status = status_word(a.device().index()).data_ptr<int32_t>();
   check(b200k_gemm_epilogue(&g, stream_of(a)), "gemm_epilogue");
   return out;
@@ -318,7 +328,7 @@ TORCH_LIBRARY(b200, m) {
   m.def("pointwise(Tensor[] inputs, int[] code, float[] imm, int[] out_shape, ScalarType out_dtype) -> Tensor");
   m.def(
       "gemm_epilogue(Tensor a, Tensor b, Tensor[] extras, int[] code, float[] imm, int[] out_shape, "
-      "ScalarType out_dtype) -> Tensor");
+      "ScalarType out_dtype, int[] form=[]) -> Tensor");
   m.def("rms_norm(Tensor x, Tensor? weight, float eps, int flags, ScalarType out_dtype) -> Tensor");
   m.def("rms_norm_swiglu(Tensor x, Tensor? weight, float eps, int flags, ScalarType out_dtype) -> Tensor");
   m.def(
