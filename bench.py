@@ -1,7 +1,7 @@
 """Benchmark: fused GEMM + epilogue sweep on B200 (the headline workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload sweep|chain|vit|llama]
+                    [--workload sweep|gemm|chain|vit|llama] [--backend ours|eager|reference_triton|inductor]
 
 One step of the default workload ("gemm_epilogue_sweep") runs the fused bf16
 GEMM sweep once: Y = act(X W^T + b) + R for act in {none, gelu, silu} and
@@ -34,8 +34,22 @@ import time
 import torch
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "torch-compile-backend_b200"))
 sys.path.insert(0, ROOT)
+
+
+def _use_ours() -> None:
+    p = os.path.join(ROOT, "torch-compile-backend_b200")
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+
+def _use_reference_triton() -> None:
+    """The unmodified reference backend installed in baseline/_ref (its package
+    is also called `compiler`, so it runs in a process of its own)."""
+    p = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(p, "compiler")):
+        raise RuntimeError("reference not installed in baseline/_ref")
+    sys.path.insert(0, p)
 
 SWEEP = [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 14336)]
 ACTS = ["none", "gelu", "silu"]
@@ -177,6 +191,7 @@ def _sweep_problems(dev, gen):
 def _pass_program(block, x, r):
     """The (code, imm) the FX passes build for this block: compile it with a
     backend that keeps the rewritten graph and read the fused node's args."""
+    _use_ours()
     from torch._decomp import get_decompositions
     from torch._dynamo.backends.common import aot_autograd
 
@@ -210,6 +225,7 @@ def _smi_id(local: int) -> str:
 
 
 def run_sweep(args, dist: Dist) -> dict:
+    _use_ours()
     from compiler import runtime
     from compiler.backend import custom_backend
 
@@ -346,6 +362,7 @@ def run_sweep(args, dist: Dist) -> dict:
 def run_single_gemm(args, dist: Dist) -> dict:
     """One sweep point on its own: --shape M,N,K --act none|gelu|silu [--tile-config c].
     Used for ncu captures and for measuring the tile table."""
+    _use_ours()
     from bench_models import GemmEpilogueBlock, init_sweep_block
     from compiler import runtime
 
@@ -403,6 +420,136 @@ def run_single_gemm(args, dist: Dist) -> dict:
             "back_to_back_us_per_call": round(wall_us, 1)}
 
 
+def _backend(name: str):
+    if name == "eager":
+        return None
+    if name == "ours":
+        _use_ours()
+        from compiler.backend import custom_backend
+
+        return custom_backend
+    if name == "reference_triton":
+        _use_reference_triton()
+        from compiler.backend import custom_backend
+
+        return custom_backend
+    if name == "inductor":
+        return "inductor"
+    raise ValueError(name)
+
+
+def _time_device(fn, steps: int, warmup: int, flush=None) -> list[float]:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        if flush is not None:
+            flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        times.append(e0.elapsed_time(e1))
+    return times
+
+
+def run_model(args, dist: Dist) -> dict:
+    """ViT-B/16 (batch 64) or Llama-style prefill (8 x 2048) forward, tokens/s,
+    with --backend eager | ours | reference_triton | inductor."""
+    import bench_models as bm
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    torch.manual_seed(0)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    if args.workload == "vit":
+        model = bm.ViT().to(dev, torch.bfloat16).eval()
+        x = torch.randn(args.batch or 64, 3, 224, 224, device=dev, generator=gen).to(torch.bfloat16)
+        tokens = x.shape[0] * 197
+        flops = bm.vit_flops_per_image() * x.shape[0]
+        cfg = {"workload": "vit_b16_forward", "batch": x.shape[0], "tokens": tokens}
+    else:
+        model = bm.Llama()
+        bm.init_normal_(model, 0.02, torch.Generator().manual_seed(0))
+        model = model.to(dev, torch.bfloat16).eval()
+        x = torch.randint(0, 128256, (args.batch or 8, 2048), device=dev, generator=gen)
+        tokens = x.numel()
+        flops = bm.llama_flops_per_token() * tokens
+        cfg = {"workload": "llama_prefill_forward", "batch": x.shape[0], "seq": 2048, "tokens": tokens}
+    be = _backend(args.backend)
+    t0 = time.perf_counter()
+    f = model if be is None else torch.compile(model, backend=be)
+    with torch.no_grad():
+        f(x)
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        times = _time_device(lambda: f(x), args.steps, args.warmup)
+    ms = statistics.median(times)
+    return {"metric": "forward tokens/s", "value": round(tokens / (ms * 1e-3), 1), "unit": "tokens/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "dtype": "bf16", "data": "synthetic, random init",
+            "config": dict(cfg, backend=args.backend),
+            "tflops": round(flops / (ms * 1e-3) / 1e12, 1), "compile_s": round(compile_s, 1)}
+
+
+def run_chain(args, dist: Dist) -> dict:
+    """RMSNorm -> split -> SiLU(gate)*up on h[16384, 8192] and softmax over
+    [32768, 4096] (bf16), through the compiled graph; GB/s of algorithmic
+    traffic (one read of the input, one write of the output)."""
+    import torch.nn.functional as F
+
+    import bench_models as bm
+
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    class RMSSwiGLU(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.norm = bm.RMSNorm(8192, 1e-6)
+
+        def forward(self, h):
+            y = self.norm(h)
+            g, u = y.split(4096, dim=-1)
+            return F.silu(g) * u
+
+    class Softmax(torch.nn.Module):
+        def forward(self, z):
+            return torch.softmax(z, -1)
+
+    m = RMSSwiGLU().to(dev)
+    with torch.no_grad():
+        m.norm.weight.copy_(1 + 0.02 * torch.randn(8192, device=dev, generator=gen))
+    m = m.to(torch.bfloat16)
+    h = torch.randn(16384, 8192, device=dev, generator=gen).to(torch.bfloat16)
+    z = (2.0 * torch.randn(32768, 4096, device=dev, generator=gen)).to(torch.bfloat16)
+    be = _backend(args.backend)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    out = {}
+    with torch.no_grad():
+        for name, mod, inp, nbytes in (("rmsnorm_swiglu", m, h, 16384 * 8192 * 2 + 8192 * 2 + 16384 * 4096 * 2),
+                                       ("softmax", Softmax(), z, 2 * 32768 * 4096 * 2)):
+            torch._dynamo.reset()
+            f = mod if be is None else torch.compile(mod, backend=be)
+            times = _time_device(lambda: f(inp), args.steps, args.warmup, flush)
+            ms = statistics.median(times)
+            out[name] = {"ms": round(ms, 4), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes": nbytes}
+    peaks, src = load_peaks()
+    tot_bytes = sum(v["bytes"] for v in out.values())
+    tot_ms = sum(v["ms"] for v in out.values())
+    gbs = tot_bytes / (tot_ms * 1e-3) / 1e9
+    return {"metric": "pointwise/reduction chain GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms, 4), "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic", "config": {"workload": "rmsnorm_swiglu+softmax",
+                                                             "backend": args.backend},
+            "kernels": out, "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3),
+                                         "peak_source": src + " hbm_gbs"}}
+
+
 # --------------------------------------------------------------- CPU (oracle) leg
 def cpu_sweep(rows: int, reps: int) -> dict:
     """The oracle's GEMM + epilogue (numpy fp32, every host core via BLAS) on
@@ -443,7 +590,10 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm", "vit", "llama", "chain"])
+    ap.add_argument("--backend", default="ours", choices=["ours", "eager", "reference_triton", "inductor"],
+                    help="vit/llama/chain workloads: which torch.compile backend runs the model")
+    ap.add_argument("--batch", type=int, default=0, help="vit/llama batch (default: the benchmark config)")
     ap.add_argument("--shape", default="4096,4096,4096", help="M,N,K for --workload gemm")
     ap.add_argument("--act", default="gelu", choices=ACTS, help="epilogue activation for --workload gemm")
     ap.add_argument("--tile-config", type=int, default=-1, help="force a GEMM tile config (gemm workload)")
@@ -472,6 +622,12 @@ def main() -> None:
     try:
         if args.workload == "gemm":
             print(json.dumps(run_single_gemm(args, dist)))
+            return
+        if args.workload in ("vit", "llama"):
+            print(json.dumps(run_model(args, dist)))
+            return
+        if args.workload == "chain":
+            print(json.dumps(run_chain(args, dist)))
             return
         res = run_sweep(args, dist)
         if dist.rank == 0:

@@ -287,3 +287,17 @@ def test_llama_gate_up_epilogue_is_canonical():
 
     forms = [list(n.args[7]) for n in _epi_nodes(SwiGLU().to(torch.bfloat16), (torch.randn(2, 8, 64).to(torch.bfloat16),))]
     assert [1, -1, 3, 2, 0, -1] in forms
+
+
+def test_pointwise_keeps_permuted_layout():
+    """An elementwise chain on a transposed view keeps ATen's output layout."""
+    class Rope(nn.Module):
+        def forward(self, q, c, s):
+            q = q.transpose(1, 2)
+            return q * c + torch.neg(q) * s
+
+    q = torch.randn(2, 8, 4, 16)
+    c = torch.randn(8, 16)
+    (gm,) = fused_graphs(Rope(), (q, c, c))
+    n = next(n for n in gm.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.pointwise.default)
+    assert list(n.args[5]) == list(n.meta["val"].stride()) and not n.meta["val"].is_contiguous()

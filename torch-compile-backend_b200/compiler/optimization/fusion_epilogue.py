@@ -184,6 +184,8 @@ def fuse_epilogue(gm: fx.GraphModule) -> fx.GraphModule:
         mat1, mat2 = matmul.args[-2:]
         root = group[-1]
         out_meta = _tensor_meta(root)
+        if not out_meta.is_contiguous():
+            continue  # the kernel writes a row-major [M, N] output
         if not _kernel_supports(mat1, mat2, out_meta, [_tensor_meta(n) for n in inputs], out_meta.shape):
             continue
         try:

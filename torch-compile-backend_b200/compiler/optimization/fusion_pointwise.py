@@ -141,6 +141,17 @@ def _inputs_supported(inputs: list[fx.Node], out_rank: int) -> bool:
     return True
 
 
+def _dense(v: torch.Tensor) -> bool:
+    """Non-overlapping and dense: a permutation of a contiguous layout."""
+    dims = sorted((d for d in range(v.dim()) if v.shape[d] != 1), key=lambda d: v.stride(d))
+    expect = 1
+    for d in dims:
+        if v.stride(d) != expect:
+            return False
+        expect *= v.shape[d]
+    return True
+
+
 def build_fused_op(group: list[fx.Node], inputs: list[fx.Node]):
     """The lowered form of a group: (target op, constant args) for
     ``torch.ops.b200.pointwise(inputs, code, imm, out_shape, out_dtype)``.
@@ -164,9 +175,17 @@ def fuse_pointwise(gm: fx.GraphModule) -> fx.GraphModule:
             prog, shape, dtype = build_fused_op(group, inputs)
         except ProgramError:
             continue
+        # Keep the layout the ATen ops would have produced (they follow their
+        # inputs' memory order); later views in the graph may rely on it.
+        if out_meta.is_contiguous():
+            stride = []
+        elif _dense(out_meta):
+            stride = [int(s) for s in out_meta.stride()]
+        else:
+            continue
         with gm.graph.inserting_before(root):
             new_node = gm.graph.call_function(
-                torch.ops.b200.pointwise.default, (list(inputs), prog.code, prog.imm, shape, dtype)
+                torch.ops.b200.pointwise.default, (list(inputs), prog.code, prog.imm, shape, dtype, stride)
             )
         new_node.meta = dict(root.meta)
         new_node.meta["b200_kernel"] = new_kernel_name("fused")

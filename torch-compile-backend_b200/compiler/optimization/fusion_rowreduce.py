@@ -147,7 +147,7 @@ def _match_rmsnorm(mean: fx.Node):
             weight = w
             out = nxt
             removed.append(nxt)
-    if _tensor_meta(out).dtype not in config.ROW_DTYPES:
+    if _tensor_meta(out).dtype not in config.ROW_DTYPES or not _tensor_meta(out).is_contiguous():
         return None
     return x, weight, eps, flags, out, removed
 
@@ -206,7 +206,7 @@ def _match_swiglu(y: fx.Node):
     if not (nxt is not None and _is(nxt, aten.mul.Tensor) and _other(nxt, s_out) is up and _only_user(up) is nxt):
         return None
     out_v = _tensor_meta(nxt)
-    if out_v is None or out_v.dtype != yv.dtype:
+    if out_v is None or out_v.dtype != yv.dtype or not out_v.is_contiguous():
         return None
     if yv.dtype != torch.float32:
         flags |= ROWF_ROUND_AFFINE
@@ -274,7 +274,8 @@ def fuse_rowreduce(gm: fx.GraphModule) -> fx.GraphModule:
         elif node.target in (aten._softmax.default, aten._log_softmax.default):
             x, dim, half_to_float = node.args
             xv = _tensor_meta(x)
-            if _rows_ok(xv) and dim in (-1, xv.dim() - 1) and not (half_to_float and xv.dtype == torch.float32):
+            if (_rows_ok(xv) and xv.is_contiguous() and dim in (-1, xv.dim() - 1)
+                    and not (half_to_float and xv.dtype == torch.float32)):
                 log = node.target == aten._log_softmax.default
                 node.target = torch.ops.b200.log_softmax.default if log else torch.ops.b200.softmax.default
                 node.meta["b200_kernel"] = new_kernel_name("log_softmax" if log else "softmax")

@@ -41,7 +41,9 @@ def _register_fakes() -> None:
     lib = "b200::"
 
     @torch.library.register_fake(lib + "pointwise")
-    def _(inputs, code, imm, out_shape, out_dtype):
+    def _(inputs, code, imm, out_shape, out_dtype, out_stride=()):
+        if out_stride:
+            return inputs[0].new_empty_strided(out_shape, out_stride, dtype=out_dtype)
         return inputs[0].new_empty(out_shape, dtype=out_dtype)
 
     @torch.library.register_fake(lib + "gemm_epilogue")

@@ -116,13 +116,17 @@ struct Dim {
   int64_t stride[B200K_MAX_INPUTS + 1];  // inputs..., output last
 };
 
-template <typename K>
-int launch_grid_stride(K kernel, const PwParams& p, int64_t units, cudaStream_t stream) {
-  int dev = 0, sms = 0, per_sm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return B200K_ERR_DEVICE;
-  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return B200K_ERR_DEVICE;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, 256, 0) != cudaSuccess) return B200K_ERR_LAUNCH;
-  per_sm = std::max(per_sm, 1);
+template <int VEC, bool I64>
+int launch_grid_stride(const PwParams& p, int64_t units, cudaStream_t stream) {
+  auto kernel = pointwise_kernel<VEC, I64>;
+  const int sms = device_sm_count();
+  if (sms <= 0) return B200K_ERR_DEVICE;
+  static int per_sm = 0;  // resident CTAs per SM for this instantiation (device-independent here)
+  if (per_sm == 0) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, 256, 0) != cudaSuccess) return B200K_ERR_LAUNCH;
+    per_sm = std::max(v, 1);
+  }
   const int64_t want = (units + 255) / 256;
   const int64_t cap = static_cast<int64_t>(sms) * per_sm;
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min(want, cap)));
@@ -236,10 +240,6 @@ extern "C" int b200k_pointwise(const B200kPointwiseArgs* a, void* stream_) {
     for (int d = 0; d < nm; ++d) p.div[d] = make_fastdiv(static_cast<uint32_t>(p.sizes[d]));
   }
 
-  if (vec) {
-    return i64 ? launch_grid_stride(pointwise_kernel<8, true>, p, units, stream)
-               : launch_grid_stride(pointwise_kernel<8, false>, p, units, stream);
-  }
-  return i64 ? launch_grid_stride(pointwise_kernel<1, true>, p, units, stream)
-             : launch_grid_stride(pointwise_kernel<1, false>, p, units, stream);
+  if (vec) return i64 ? launch_grid_stride<8, true>(p, units, stream) : launch_grid_stride<8, false>(p, units, stream);
+  return i64 ? launch_grid_stride<1, true>(p, units, stream) : launch_grid_stride<1, false>(p, units, stream);
 }

@@ -13,6 +13,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/library.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -67,27 +68,49 @@ at::Tensor& status_word(int dev) {
   return words[dev];
 }
 
+// out_stride (optional) gives the output the layout the replaced ATen op would
+// have produced (elementwise ops keep their inputs' memory order); it must be
+// a dense permutation of a contiguous layout.  The kernel then iterates the
+// dims in output-stride order, so it still writes the output densely.
 at::Tensor pointwise(at::TensorList inputs, at::IntArrayRef code, at::ArrayRef<double> imm,
-                     at::IntArrayRef out_shape, at::ScalarType out_dtype) {
+                     at::IntArrayRef out_shape, at::ScalarType out_dtype, at::IntArrayRef out_stride) {
   TORCH_CHECK(!inputs.empty() && inputs.size() <= B200K_MAX_INPUTS, "b200::pointwise: 1..8 inputs, got ",
               inputs.size());
-  TORCH_CHECK(static_cast<int64_t>(out_shape.size()) <= B200K_MAX_DIMS, "b200::pointwise: rank > 6");
+  const int rank = static_cast<int>(out_shape.size());
+  TORCH_CHECK(rank <= B200K_MAX_DIMS, "b200::pointwise: rank > 6");
+  TORCH_CHECK(out_stride.empty() || static_cast<int>(out_stride.size()) == rank,
+              "b200::pointwise: out_stride rank mismatch");
   const at::Tensor& first = inputs[0];
   TORCH_CHECK(first.is_cuda(), "b200::pointwise: inputs must be CUDA tensors");
   c10::cuda::CUDAGuard guard(first.device());
-  at::Tensor out = at::empty(out_shape, first.options().dtype(out_dtype));
+  at::Tensor out = out_stride.empty() ? at::empty(out_shape, first.options().dtype(out_dtype))
+                                      : at::empty_strided(out_shape, out_stride, first.options().dtype(out_dtype));
+  // Iteration order: dims sorted by output stride, largest first (identity when contiguous).
+  std::vector<int> perm(rank);
+  for (int d = 0; d < rank; ++d) perm[d] = d;
+  if (!out_stride.empty()) {
+    std::stable_sort(perm.begin(), perm.end(), [&](int x, int y) {
+      return out.stride(x) > out.stride(y) || (out.stride(x) == out.stride(y) && out.size(x) > out.size(y));
+    });
+    int64_t expect = 1;
+    for (int k = rank - 1; k >= 0; --k) {
+      const int d = perm[k];
+      TORCH_CHECK(out.size(d) == 1 || out.stride(d) == expect, "b200::pointwise: out_stride is not dense");
+      expect *= out.size(d);
+    }
+  }
   B200kPointwiseArgs a;
   std::memset(&a, 0, sizeof(a));
-  a.rank = static_cast<int32_t>(out_shape.size());
+  a.rank = rank;
   a.n_inputs = static_cast<int32_t>(inputs.size());
-  for (int d = 0; d < a.rank; ++d) a.sizes[d] = out_shape[d];
+  for (int k = 0; k < rank; ++k) a.sizes[k] = out_shape[perm[k]];
   for (size_t i = 0; i < inputs.size(); ++i) {
     const at::Tensor& t = inputs[i];
     TORCH_CHECK(t.is_cuda() && t.device() == first.device(), "b200::pointwise: inputs on different devices");
     const at::Tensor e = t.expand(out_shape);
     a.inputs[i].ptr = e.data_ptr();
     a.inputs[i].dtype = to_dt(e.scalar_type());
-    for (int d = 0; d < a.rank; ++d) a.inputs[i].strides[d] = e.stride(d);
+    for (int k = 0; k < rank; ++k) a.inputs[i].strides[k] = e.stride(perm[k]);
   }
   a.out = out.data_ptr();
   a.out_dtype = to_dt(out_dtype);
@@ -325,7 +348,9 @@ at::Tensor log_softmax(const at::Tensor& x, int64_t dim, bool half_to_float) {
 }  // namespace
 
 TORCH_LIBRARY(b200, m) {
-  m.def("pointwise(Tensor[] inputs, int[] code, float[] imm, int[] out_shape, ScalarType out_dtype) -> Tensor");
+  m.def(
+      "pointwise(Tensor[] inputs, int[] code, float[] imm, int[] out_shape, ScalarType out_dtype, "
+      "int[] out_stride=[]) -> Tensor");
   m.def(
       "gemm_epilogue(Tensor a, Tensor b, Tensor[] extras, int[] code, float[] imm, int[] out_shape, "
       "ScalarType out_dtype, int[] form=[]) -> Tensor");
