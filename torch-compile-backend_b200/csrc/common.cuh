@@ -18,7 +18,12 @@ namespace b200k {
 // sigmoid = 1/(1+exp(-x)), tanh = 2*sigmoid(2x)-1, relu/max/min keep the
 // non-NaN operand (Triton's default maximum/minimum).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float op_sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// exp, log: the hardware ex2/lg2 approximations (a few ulp), which is also
+// what the reference's tl.exp / tl.log lower to; erf, sqrt and division stay
+// IEEE-accurate.
+__device__ __forceinline__ float op_exp(float x) { return __expf(x); }
+__device__ __forceinline__ float op_log(float x) { return __logf(x); }
+__device__ __forceinline__ float op_sigmoid(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float op_tanh(float x) { return 2.0f * op_sigmoid(2.0f * x) - 1.0f; }
 __device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 __device__ __forceinline__ float round_f16(float x) { return __half2float(__float2half_rn(x)); }
@@ -189,8 +194,8 @@ __device__ __forceinline__ void run_program(const B200kProgram& prog, float (&r)
       B200K_UN_CASE(B200K_OP_NEG, -a)
       B200K_UN_CASE(B200K_OP_ABS, fabsf(a))
       B200K_UN_CASE(B200K_OP_RELU, fmaxf(a, 0.0f))
-      B200K_UN_CASE(B200K_OP_EXP, expf(a))
-      B200K_UN_CASE(B200K_OP_LOG, logf(a))
+      B200K_UN_CASE(B200K_OP_EXP, op_exp(a))
+      B200K_UN_CASE(B200K_OP_LOG, op_log(a))
       B200K_UN_CASE(B200K_OP_SQRT, sqrtf(a))
       B200K_UN_CASE(B200K_OP_RSQRT, rsqrtf(a))
       B200K_UN_CASE(B200K_OP_ERF, erff(a))

@@ -72,6 +72,8 @@ struct Params {
   int64_t timeout_ns;
   uint32_t idesc;
   int32_t f_bias, f_act, f_round, f_scale, f_res;  // canonical epilogue form (fast path)
+  int32_t xm_bias, xm_scale, xm_res;               // how the fast path stages each operand (XM_*)
+  int32_t pad2;
   EpiOperand ex[B200K_MAX_INPUTS - 1];
   B200kProgram prog;
 };
@@ -367,62 +369,210 @@ __device__ __forceinline__ void apply_act8(int act, float (&v)[8]) {
   }
 }
 
-using FastRegs = float[3][8];  // bias, scale, residual for one 8-column group
+// ------------------------------------------- fast path, latency-hiding loop
+// Operand staging modes, chosen on the host per operand:
+//   XM_BCAST   row-broadcast vector (stride_m == 0, e.g. a bias): each lane
+//              loads one column of the 32-column sub-chunk (one coalesced
+//              load per warp) and the values reach every row by __shfl_sync;
+//   XM_ROW16   full 16-bit matrix with unit column stride (a residual, or the
+//              `up` operand of SwiGLU): each lane loads its own row's 32
+//              values (64 bytes) into registers;
+//   XM_GENERIC anything else: loaded per 8-column group when needed.
+// BCAST and ROW16 operands are prefetched one 32-column sub-chunk ahead,
+// across tile boundaries, so their DRAM latency overlaps the current
+// sub-chunk's arithmetic.
+enum { XM_NONE = 0, XM_BCAST = 1, XM_ROW16 = 2, XM_GENERIC = 3 };
 
-__device__ __forceinline__ void load_fast(const Params& p, int m, int n, FastRegs& x) {
-  if (p.f_bias >= 0) load_extra8(p.ex[p.f_bias], m, n, p.M, p.N, x[0]);
-  if (p.f_scale >= 0) load_extra8(p.ex[p.f_scale], m, n, p.M, p.N, x[1]);
-  if (p.f_res >= 0) load_extra8(p.ex[p.f_res], m, n, p.M, p.N, x[2]);
+struct FastOps {
+  float bias_b, scale_b, res_b;
+  uint4 scale_r[4], res_r[4];
+};
+
+// 32 lanes x 32 bit, 32 consecutive columns.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
 }
 
-template <int OUT_BYTES>
-__device__ __forceinline__ void epilogue_group_fast(const Params& p, uint32_t taddr, int m, int n, int g, int lane,
-                                                    uint8_t* sb, const FastRegs& cur, FastRegs& nxt, bool prefetch) {
-  uint32_t raw[8];
-  tmem_ld8(taddr, raw);
-  if (prefetch) load_fast(p, m, n + 8, nxt);
-  tmem_wait_ld();
-  float v[8];
+__device__ __forceinline__ float load_bcast(const EpiOperand& e, int n, int lane, int N) {
+  const int col = n + lane;
+  return col < N ? load_scalar(e.ptr, static_cast<int64_t>(col) * e.sn, e.dt) : 0.0f;
+}
+
+__device__ __forceinline__ void load_row16(const EpiOperand& e, int m, int n, int M, int N, uint4 (&b)[4]) {
+  const uint16_t* base = reinterpret_cast<const uint16_t*>(e.ptr);
+  if (m < M && n + 32 <= N) {
+    const uint4* q = reinterpret_cast<const uint4*>(base + static_cast<int64_t>(m) * e.sm + n);
 #pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[j]);
-  if (p.f_bias >= 0) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] += cur[0][j];
-  }
-  apply_act8(p.f_act, v);
-  if (p.f_round == B200K_BF16) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
-  } else if (p.f_round == B200K_F16) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
-  }
-  if (p.f_scale >= 0) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] *= cur[1][j];
-  }
-  if (p.f_res >= 0) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] += cur[2][j];
-  }
-  if (p.direct_store) {
-    if (m < p.M) {
-      const int64_t off = static_cast<int64_t>(m) * p.out_sm + n;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (n + j < p.N) store_scalar(p.out, off + j, p.out_dt, v[j]);
-    }
-  } else if (OUT_BYTES == 2) {
-    const uint4 u = (p.out_dt == B200K_BF16) ? pack_bf16x8(v) : pack_f16x8(v);
-    *reinterpret_cast<uint4*>(sb + lane * 128 + ((g ^ (lane & 7)) << 4)) = u;
+    for (int i = 0; i < 4; ++i) b[i] = __ldg(q + i);
   } else {
+    uint32_t w[16];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int chunk = 2 * g + h;
-      *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
-          make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+    for (int j = 0; j < 16; ++j) {
+      const uint32_t lo = (m < M && n + 2 * j < N) ? base[static_cast<int64_t>(m) * e.sm + n + 2 * j] : 0u;
+      const uint32_t hi = (m < M && n + 2 * j + 1 < N) ? base[static_cast<int64_t>(m) * e.sm + n + 2 * j + 1] : 0u;
+      w[j] = lo | (hi << 16);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+  }
+}
+
+__device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, int lane, FastOps& f) {
+  if (p.xm_bias == XM_BCAST) f.bias_b = load_bcast(p.ex[p.f_bias], n, lane, p.N);
+  if (p.xm_scale == XM_BCAST) f.scale_b = load_bcast(p.ex[p.f_scale], n, lane, p.N);
+  else if (p.xm_scale == XM_ROW16) load_row16(p.ex[p.f_scale], m, n, p.M, p.N, f.scale_r);
+  if (p.xm_res == XM_BCAST) f.res_b = load_bcast(p.ex[p.f_res], n, lane, p.N);
+  else if (p.xm_res == XM_ROW16) load_row16(p.ex[p.f_res], m, n, p.M, p.N, f.res_r);
+}
+
+__device__ __forceinline__ void unpack16x8(uint4 u, int dt, float (&x)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f;
+    if (dt == B200K_BF16) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+    else f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+    x[2 * j] = f.x;
+    x[2 * j + 1] = f.y;
+  }
+}
+
+// The operand of one role for columns [n_g, n_g + 8) of the current sub-chunk (group g).
+__device__ __forceinline__ void operand8(const Params& p, int mode, int idx, float bval, const uint4 (&r)[4], int g,
+                                         int m, int n_g, float (&x)[8]) {
+  if (mode == XM_BCAST) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = __shfl_sync(0xffffffffu, bval, g * 8 + j);
+  } else if (mode == XM_ROW16) {
+    unpack16x8(r[g], p.ex[idx].dt, x);
+  } else {
+    load_extra8(p.ex[idx], m, n_g, p.M, p.N, x);
+  }
+}
+
+template <int BN, int OUT_BYTES>
+__device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
+                                                   uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
+                                                   int half, int lane, const Ctl& ctl) {
+  constexpr int kEC = 128 / OUT_BYTES;     // output columns per 128-byte staging row
+  constexpr int NSUB = (BN / 2) / 32;      // 32-column sub-chunks per warp and tile
+  constexpr int SUB_PER_STG = kEC / 32;    // sub-chunks per staging row
+  FastOps ops[2];
+  int cur = 0;
+  if (static_cast<int>(blockIdx.x) < p.num_tiles) {
+    int tm, tn;
+    tile_coords(blockIdx.x, p, tm, tn);
+    fast_prefetch(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2), lane, ops[0]);
+  }
+  int acc = 0;
+  uint32_t aph = 0;
+  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x) {
+    int tm, tn;
+    tile_coords(t, p, tm, tn);
+    const int m = tm * BM + quarter * 32 + lane;
+    const int ncol0 = tn * BN + half * (BN / 2);
+    if (!wait_bar(&tfull[acc], aph, ctl)) break;
+    tc_fence_after();
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                           static_cast<uint32_t>(acc * BN + half * (BN / 2));
+#pragma unroll 1
+    for (int s = 0; s < NSUB; ++s) {
+      const int n = ncol0 + s * 32;
+      if (s + 1 < NSUB) {
+        fast_prefetch(p, m, n + 32, lane, ops[cur ^ 1]);
+      } else if (t + static_cast<int>(gridDim.x) < p.num_tiles) {
+        int tm2, tn2;
+        tile_coords(t + gridDim.x, p, tm2, tn2);
+        fast_prefetch(p, tm2 * BM + quarter * 32 + lane, tn2 * BN + half * (BN / 2), lane, ops[cur ^ 1]);
+      }
+      if (n < p.N) {
+        uint32_t raw[32];
+        tmem_ld32(t_row + s * 32, raw);
+        tmem_wait_ld();
+        const int sub = s % SUB_PER_STG;
+        if (sub == 0 && !p.direct_store) {
+          if (lane == 0) bulk_wait_read_all();
+          __syncwarp();
+        }
+        const FastOps& o = ops[cur];
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int ng = n + g * 8;
+          float v[8], x[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[g * 8 + j]);
+          if (p.f_bias >= 0) {
+            operand8(p, p.xm_bias, p.f_bias, o.bias_b, o.res_r, g, m, ng, x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += x[j];
+          }
+          apply_act8(p.f_act, v);
+          if (p.f_round == B200K_BF16) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
+          } else if (p.f_round == B200K_F16) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
+          }
+          if (p.f_scale >= 0) {
+            operand8(p, p.xm_scale, p.f_scale, o.scale_b, o.scale_r, g, m, ng, x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] *= x[j];
+          }
+          if (p.f_res >= 0) {
+            operand8(p, p.xm_res, p.f_res, o.res_b, o.res_r, g, m, ng, x);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) v[j] += x[j];
+          }
+          if (p.direct_store) {
+            if (m < p.M) {
+              const int64_t off = static_cast<int64_t>(m) * p.out_sm + ng;
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                if (ng + j < p.N) store_scalar(p.out, off + j, p.out_dt, v[j]);
+            }
+          } else if (OUT_BYTES == 2) {
+            const uint4 u = (p.out_dt == B200K_BF16) ? pack_bf16x8(v) : pack_f16x8(v);
+            const int chunk = sub * 4 + g;
+            *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u;
+          } else {
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int chunk = 2 * g + h;
+              *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+            }
+          }
+        }
+        if (!p.direct_store && (sub == SUB_PER_STG - 1 || s + 1 == NSUB || n + 32 >= p.N)) {
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tmO, sb, n - sub * 32, tm * BM + quarter * 32);
+            bulk_commit();
+          }
+        }
+      }
+      cur ^= 1;
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&tempty[acc]);
+    if (++acc == 2) {
+      acc = 0;
+      aph ^= 1u;
     }
   }
+  if (!p.direct_store && lane == 0) bulk_wait_all();
+  __syncwarp();
 }
 
 template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
@@ -573,8 +723,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       wait_bar_drain(drain, 0, 100000000ull);
     }
     __syncwarp();
+  } else if (warp >= 4 && FAST) {
+    // ------------------------------------------------------------ epilogue (compiled form)
+    const int ew = warp - 4;
+    epilogue_fast_loop<BN, OUT_BYTES>(p, &tmO, tmem_base, tfull, tempty, sStg + ew * kStgBytes, warp & 3, ew >> 2,
+                                      lane, ctl);
   } else if (warp >= 4) {
-    // ------------------------------------------------------------ epilogue
+    // ------------------------------------------------------------ epilogue (interpreted program)
     // Warp w reads TMEM lane quarter (w % 4) and one half of the tile's columns.
     const int ew = warp - 4;
     const int quarter = warp & 3;
@@ -599,16 +754,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) bulk_wait_read_all();
           __syncwarp();
         }
-        if constexpr (FAST) {
-          FastRegs xa, xb;
-          load_fast(p, m, n0, xa);
-#pragma unroll 1
-          for (int g = 0; g < C::kEC / 8; g += 2) {
-            epilogue_group_fast<OUT_BYTES>(p, t_row + c * C::kEC + g * 8, m, n0 + g * 8, g, lane, sb, xa, xb, true);
-            epilogue_group_fast<OUT_BYTES>(p, t_row + c * C::kEC + (g + 1) * 8, m, n0 + (g + 1) * 8, g + 1, lane, sb,
-                                           xb, xa, g + 2 < C::kEC / 8);
-          }
-        } else {
+        {
           ExtraRegs xa, xb;
           load_extras(p, m, n0, xa);
 #pragma unroll 1
@@ -868,6 +1014,18 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.f_round = a->form.round;
   p.f_scale = a->form.scale;
   p.f_res = a->form.residual;
+  auto mode_of = [&](int idx, bool allow_row) -> int32_t {
+    if (idx < 0) return XM_NONE;
+    const B200kEpiOperand& e = a->extras[idx];
+    if (e.stride_m == 0) return XM_BCAST;
+    if (allow_row && e.stride_n == 1 && (e.dtype == B200K_BF16 || e.dtype == B200K_F16) && aligned16(e.ptr) &&
+        e.stride_m % 8 == 0)
+      return XM_ROW16;
+    return XM_GENERIC;
+  };
+  p.xm_bias = mode_of(a->form.bias, false);
+  p.xm_scale = mode_of(a->form.scale, true);
+  p.xm_res = mode_of(a->form.residual, true);
 
   CUtensorMap ta, tb, to;
   std::memset(&to, 0, sizeof(to));

@@ -66,6 +66,43 @@ __device__ __forceinline__ float row_allreduce(float v, float* sm) {
   return v;
 }
 
+// A vector of VEC row elements as held in registers between the reduction
+// and the output pass: 16-bit inputs stay packed (one 16-byte register
+// quad per 8 elements), which halves the registers a row needs and doubles
+// the resident rows per SM.
+template <int VEC, bool X16>
+struct RowFrag {
+  float v[VEC];
+  __device__ __forceinline__ void load(const void* base, int64_t off, int dt) {
+    if constexpr (VEC == 8) {
+      load_vec8(base, off, dt, v);
+    } else {
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) v[j] = load_scalar(base, off + j, dt);
+    }
+  }
+  __device__ __forceinline__ float get(int j, int) const { return v[j]; }
+  __device__ __forceinline__ void zero() {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) v[j] = 0.0f;
+  }
+};
+
+template <>
+struct RowFrag<8, true> {
+  uint4 u;
+  __device__ __forceinline__ void load(const void* base, int64_t off, int) {
+    u = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(base) + off));
+  }
+  __device__ __forceinline__ float get(int j, int dt) const {
+    const uint32_t w = (j < 2) ? u.x : (j < 4) ? u.y : (j < 6) ? u.z : u.w;
+    const uint32_t h = (j & 1) ? (w >> 16) : (w & 0xffffu);
+    if (dt == B200K_BF16) return __uint_as_float(h << 16);
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(h)));
+  }
+  __device__ __forceinline__ void zero() { u = make_uint4(0, 0, 0, 0); }
+};
+
 template <int VEC>
 __device__ __forceinline__ void load_row_vec(const void* base, int64_t off, int dt, float (&v)[VEC]) {
   if constexpr (VEC == 8) {
@@ -91,30 +128,38 @@ __device__ __forceinline__ float round_to(float x, int dt) {
   return x;
 }
 
+__host__ __device__ constexpr int threads_for(int tpr) { return tpr >= 256 ? tpr : 256; }
+
 // ---------------------------------------------------------------------------
 // RMSNorm / LayerNorm:  y = affine(normalise(x))
 // ---------------------------------------------------------------------------
-template <int TPR, int VEC, bool LAYER>
-__global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rownorm_kernel(const __grid_constant__ RowParams p) {
-  constexpr int RPB = TPR >= 256 ? 1 : 256 / TPR;
-  __shared__ float sm[(TPR >= 256 ? TPR : 256) / 32];
+template <int TPR, int VEC, bool LAYER, bool X16>
+__global__ void __launch_bounds__(threads_for(TPR)) rownorm_kernel(const __grid_constant__ RowParams p) {
+  constexpr int RPB = threads_for(TPR) / TPR;
+  __shared__ float sm[threads_for(TPR) / 32];
   const int lane = threadIdx.x % TPR;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + threadIdx.x / TPR;
   const bool valid_row = row < p.rows;
   const int64_t nvec = p.cols / VEC;
+  const int dt = p.x_dt;
 
-  float v[kVPT][VEC];
+  RowFrag<VEC, X16> f[kVPT];
   float s = 0.0f;
 #pragma unroll
   for (int k = 0; k < kVPT; ++k) {
     const int64_t vi = lane + k * TPR;
     if (valid_row && vi < nvec) {
-      load_row_vec<VEC>(p.x, row * p.x_stride + vi * VEC, p.x_dt, v[k]);
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) s += LAYER ? v[k][j] : v[k][j] * v[k][j];
+      f[k].load(p.x, row * p.x_stride + vi * VEC, dt);
     } else {
+      f[k].zero();
+    }
+  }
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) v[k][j] = 0.0f;
+  for (int k = 0; k < kVPT; ++k) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float x = f[k].get(j, dt);
+      s += LAYER ? x : x * x;
     }
   }
   s = row_allreduce<TPR, false>(s, sm);
@@ -129,7 +174,7 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rownorm_kernel(const _
       if (valid_row && vi < nvec) {
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const float d = v[k][j] - mean;
+          const float d = f[k].get(j, dt) - mean;
           q += d * d;
         }
       }
@@ -157,7 +202,7 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rownorm_kernel(const _
 #pragma unroll
         for (int j = 0; j < VEC; ++j) wv[j] = 1.0f;
       }
-      if (p.b) {
+      if (LAYER && p.b) {
         load_row_vec<VEC>(p.b, vi * VEC, p.b_dt, bv);
       } else {
 #pragma unroll
@@ -165,8 +210,8 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rownorm_kernel(const _
       }
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
-        float n = (v[k][j] - mean) * rstd;
-        if (round_normed) n = round_to(n, p.x_dt);
+        float n = (f[k].get(j, dt) - mean) * rstd;
+        if (round_normed) n = round_to(n, dt);
         const float w = plus_one ? 1.0f + wv[j] : wv[j];
         y[j] = LAYER ? n * w + bv[j] : w * n;
       }
@@ -178,26 +223,36 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rownorm_kernel(const _
 // ---------------------------------------------------------------------------
 // RMSNorm over the full row, then out[j] = silu(y[j]) * y[j + cols/2].
 // ---------------------------------------------------------------------------
-template <int TPR, int VEC>
-__global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rmsnorm_swiglu_kernel(const __grid_constant__ RowParams p) {
-  constexpr int RPB = TPR >= 256 ? 1 : 256 / TPR;
-  __shared__ float sm[(TPR >= 256 ? TPR : 256) / 32];
+template <int TPR, int VEC, bool X16>
+__global__ void __launch_bounds__(threads_for(TPR)) rmsnorm_swiglu_kernel(const __grid_constant__ RowParams p) {
+  constexpr int RPB = threads_for(TPR) / TPR;
+  __shared__ float sm[threads_for(TPR) / 32];
   const int lane = threadIdx.x % TPR;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + threadIdx.x / TPR;
   const bool valid_row = row < p.rows;
   const int64_t half = p.cols / 2;
   const int64_t nvec = half / VEC;
+  const int dt = p.x_dt;
 
-  float g[kVPT][VEC], u[kVPT][VEC];
-  float s = 0.0f;
+  RowFrag<VEC, X16> g[kVPT], u[kVPT];
 #pragma unroll
   for (int k = 0; k < kVPT; ++k) {
     const int64_t vi = lane + k * TPR;
     if (valid_row && vi < nvec) {
-      load_row_vec<VEC>(p.x, row * p.x_stride + vi * VEC, p.x_dt, g[k]);
-      load_row_vec<VEC>(p.x, row * p.x_stride + half + vi * VEC, p.x_dt, u[k]);
+      g[k].load(p.x, row * p.x_stride + vi * VEC, dt);
+      u[k].load(p.x, row * p.x_stride + half + vi * VEC, dt);
+    } else {
+      g[k].zero();
+      u[k].zero();
+    }
+  }
+  float s = 0.0f;
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) s += g[k][j] * g[k][j] + u[k][j] * u[k][j];
+  for (int k = 0; k < kVPT; ++k) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      const float a = g[k].get(j, dt), b = u[k].get(j, dt);
+      s += a * a + b * b;
     }
   }
   s = row_allreduce<TPR, false>(s, sm);
@@ -222,10 +277,10 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rmsnorm_swiglu_kernel(
       }
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
-        float ng = g[k][j] * rstd, nu = u[k][j] * rstd;
+        float ng = g[k].get(j, dt) * rstd, nu = u[k].get(j, dt) * rstd;
         if (round_normed) {
-          ng = round_to(ng, p.x_dt);
-          nu = round_to(nu, p.x_dt);
+          ng = round_to(ng, dt);
+          nu = round_to(nu, dt);
         }
         float yg = (plus_one ? 1.0f + wg[j] : wg[j]) * ng;
         float yu = (plus_one ? 1.0f + wu[j] : wu[j]) * nu;
@@ -245,24 +300,25 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) rmsnorm_swiglu_kernel(
 // ---------------------------------------------------------------------------
 // Softmax / log-softmax over the row (fp32 math, like aten._softmax).
 // ---------------------------------------------------------------------------
-template <int TPR, int VEC>
-__global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) softmax_kernel(const __grid_constant__ RowParams p) {
-  constexpr int RPB = TPR >= 256 ? 1 : 256 / TPR;
-  __shared__ float sm[(TPR >= 256 ? TPR : 256) / 32];
+template <int TPR, int VEC, bool X16>
+__global__ void __launch_bounds__(threads_for(TPR)) softmax_kernel(const __grid_constant__ RowParams p) {
+  constexpr int RPB = threads_for(TPR) / TPR;
+  __shared__ float sm[threads_for(TPR) / 32];
   const int lane = threadIdx.x % TPR;
   const int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + threadIdx.x / TPR;
   const bool valid_row = row < p.rows;
   const int64_t nvec = p.cols / VEC;
+  const int dt = p.x_dt;
 
-  float v[kVPT][VEC];
+  RowFrag<VEC, X16> f[kVPT];
   float m = -INFINITY;
 #pragma unroll
   for (int k = 0; k < kVPT; ++k) {
     const int64_t vi = lane + k * TPR;
     if (valid_row && vi < nvec) {
-      load_row_vec<VEC>(p.x, row * p.x_stride + vi * VEC, p.x_dt, v[k]);
+      f[k].load(p.x, row * p.x_stride + vi * VEC, dt);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) m = fmaxf(m, v[k][j]);
+      for (int j = 0; j < VEC; ++j) m = fmaxf(m, f[k].get(j, dt));
     }
   }
   m = row_allreduce<TPR, true>(m, sm);
@@ -272,23 +328,23 @@ __global__ void __launch_bounds__(TPR >= 256 ? TPR : 256) softmax_kernel(const _
     const int64_t vi = lane + k * TPR;
     if (valid_row && vi < nvec) {
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float e = expf(v[k][j] - m);
-        s += e;
-        if (!p.log_softmax) v[k][j] = e;
-      }
+      for (int j = 0; j < VEC; ++j) s += __expf(f[k].get(j, dt) - m);
     }
   }
   s = row_allreduce<TPR, false>(s, sm);
   if (!valid_row) return;
-  const float ls = logf(s);
+  const float inv = 1.0f / s;
+  const float ls = __logf(s);
 #pragma unroll
   for (int k = 0; k < kVPT; ++k) {
     const int64_t vi = lane + k * TPR;
     if (vi < nvec) {
       float y[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) y[j] = p.log_softmax ? (v[k][j] - m) - ls : v[k][j] / s;
+      for (int j = 0; j < VEC; ++j) {
+        const float d = f[k].get(j, dt) - m;
+        y[j] = p.log_softmax ? d - ls : __expf(d) * inv;
+      }
       store_row_vec<VEC>(p.out, row * p.out_stride + vi * VEC, p.out_dt, y);
     }
   }
@@ -304,17 +360,18 @@ int pick_tpr(int64_t nvec) {
   return 0;
 }
 
-template <template <int, int> class KSel>
-int dispatch_tpr(int tpr, bool vec, const RowParams& p, cudaStream_t st) {
+template <template <int, int, bool> class KSel>
+int dispatch_tpr(int tpr, bool vec, bool x16, const RowParams& p, cudaStream_t st) {
   const int threads = std::max(tpr, 256);
   const int rpb = tpr >= 256 ? 1 : 256 / tpr;
   const int64_t grid64 = (p.rows + rpb - 1) / rpb;
   if (grid64 > 0x7fffffff) return B200K_ERR_SHAPE;
   const int grid = static_cast<int>(grid64);
-#define B200K_LAUNCH_TPR(T)                                                         \
-  case T:                                                                           \
-    if (vec) KSel<T, 8>::fn()<<<grid, threads, 0, st>>>(p);                          \
-    else KSel<T, 1>::fn()<<<grid, threads, 0, st>>>(p);                              \
+#define B200K_LAUNCH_TPR(T)                                                          \
+  case T:                                                                            \
+    if (vec && x16) KSel<T, 8, true>::fn()<<<grid, threads, 0, st>>>(p);              \
+    else if (vec) KSel<T, 8, false>::fn()<<<grid, threads, 0, st>>>(p);               \
+    else KSel<T, 1, false>::fn()<<<grid, threads, 0, st>>>(p);                        \
     break;
   switch (tpr) {
     B200K_LAUNCH_TPR(32)
@@ -329,10 +386,10 @@ int dispatch_tpr(int tpr, bool vec, const RowParams& p, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
 }
 
-template <int T, int V> struct SelRms { static auto fn() { return rownorm_kernel<T, V, false>; } };
-template <int T, int V> struct SelLayer { static auto fn() { return rownorm_kernel<T, V, true>; } };
-template <int T, int V> struct SelSwiglu { static auto fn() { return rmsnorm_swiglu_kernel<T, V>; } };
-template <int T, int V> struct SelSoftmax { static auto fn() { return softmax_kernel<T, V>; } };
+template <int T, int V, bool X> struct SelRms { static auto fn() { return rownorm_kernel<T, V, false, X>; } };
+template <int T, int V, bool X> struct SelLayer { static auto fn() { return rownorm_kernel<T, V, true, X>; } };
+template <int T, int V, bool X> struct SelSwiglu { static auto fn() { return rmsnorm_swiglu_kernel<T, V, X>; } };
+template <int T, int V, bool X> struct SelSoftmax { static auto fn() { return softmax_kernel<T, V, X>; } };
 
 bool row_vec_ok(const void* ptr, int64_t stride, int64_t len) {
   return ptr == nullptr || (aligned16(ptr) && stride % 8 == 0 && len % 8 == 0);
@@ -386,9 +443,10 @@ extern "C" int b200k_rownorm(const B200kRowNormArgs* a, void* stream_) {
   const int tpr = pick_tpr(vec ? span / 8 : span);
   if (tpr == 0) return B200K_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  if (swiglu) return dispatch_tpr<SelSwiglu>(tpr, vec, p, st);
-  if (layer) return dispatch_tpr<SelLayer>(tpr, vec, p, st);
-  return dispatch_tpr<SelRms>(tpr, vec, p, st);
+  const bool x16 = a->x_dtype == B200K_BF16 || a->x_dtype == B200K_F16;
+  if (swiglu) return dispatch_tpr<SelSwiglu>(tpr, vec, x16, p, st);
+  if (layer) return dispatch_tpr<SelLayer>(tpr, vec, x16, p, st);
+  return dispatch_tpr<SelRms>(tpr, vec, x16, p, st);
 }
 
 extern "C" int b200k_softmax(const B200kSoftmaxArgs* a, void* stream_) {
@@ -412,5 +470,6 @@ extern "C" int b200k_softmax(const B200kSoftmaxArgs* a, void* stream_) {
   const bool vec = row_vec_ok(a->x, a->x_row_stride, a->cols) && row_vec_ok(a->out, a->out_row_stride, a->cols);
   const int tpr = pick_tpr(vec ? a->cols / 8 : a->cols);
   if (tpr == 0) return B200K_ERR_SHAPE;
-  return dispatch_tpr<SelSoftmax>(tpr, vec, p, static_cast<cudaStream_t>(stream_));
+  const bool x16 = a->x_dtype == B200K_BF16 || a->x_dtype == B200K_F16;
+  return dispatch_tpr<SelSoftmax>(tpr, vec, x16, p, static_cast<cudaStream_t>(stream_));
 }
