@@ -212,6 +212,27 @@ typedef struct {
 
 int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 
+/*
+ * b200k_gemm_epilogue for callers that cannot allocate device memory.
+ * No reference counterpart: the reference has no allocation-free entry.
+ * Hosts that run inside a graph-capture-only runtime, a plugin sandbox or a
+ * custom memory manager may be unable to call cudaMalloc; the regular entry
+ * needs them to supply the device status word (args->status).  This variant
+ * ignores args->status and uses the library's own scratch instead: a
+ * file-scope __device__ array of B200K_NOALLOC_SCRATCH_BYTES (256 bytes) that
+ * every GPU which loads the library keeps until exit.  A call needs
+ * B200K_NOALLOC_STATUS_BYTES of it (the status word, cleared on the stream
+ * before the launch); a larger need is rejected with B200K_ERR_SHAPE.
+ * The first call on a device looks up that device's copy of the array
+ * (cudaGetSymbolAddress, with the device current); make that first call
+ * before any stream capture.  All calls share the array: calls whose kernels
+ * overlap on the GPU race on the status word.  Inputs and outputs are passed
+ * as for b200k_gemm_epilogue; nothing is allocated or freed.
+ */
+#define B200K_NOALLOC_SCRATCH_BYTES 256
+#define B200K_NOALLOC_STATUS_BYTES 4
+int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream);
+
 /* Number of GEMM tile configurations in the built-in table and their shapes. */
 int b200k_gemm_num_configs(void);
 int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages);

@@ -28,6 +28,7 @@ ROW_RMSNORM, ROW_LAYERNORM, ROW_RMSNORM_SWIGLU = 0, 1, 2
 EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
+    "b200k_gemm_epilogue_noalloc",
 ]
 
 
@@ -100,6 +101,7 @@ def library() -> ctypes.CDLL:
         for name, argt in [
             ("b200k_pointwise", [ctypes.POINTER(PointwiseArgs), ctypes.c_void_p]),
             ("b200k_gemm_epilogue", [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
+            ("b200k_gemm_epilogue_noalloc", [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
             ("b200k_rownorm", [ctypes.POINTER(RowNormArgs), ctypes.c_void_p]),
             ("b200k_softmax", [ctypes.POINTER(SoftmaxArgs), ctypes.c_void_p]),
             ("b200k_gemm_pick_config", [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
@@ -163,8 +165,10 @@ def pointwise(inputs: list[torch.Tensor], code, imm, out: torch.Tensor) -> None:
 
 def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], code, imm, out: torch.Tensor,
                   tile_config: int = -1, status: torch.Tensor | None = None, timeout_ns: int = 0,
-                  form=None) -> None:
-    """out[M,N] = program(a @ b, extras) with extras given as [M,N]-broadcastable tensors."""
+                  form=None, noalloc: bool = False) -> None:
+    """out[M,N] = program(a @ b, extras) with extras given as [M,N]-broadcastable tensors.
+    noalloc=True calls b200k_gemm_epilogue_noalloc, which ignores `status` and
+    uses the library's own status scratch (for hosts that cannot allocate)."""
     g = GemmArgs()
     M, K = a.shape
     N = b.shape[1]
@@ -187,7 +191,10 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
     g.timeout_ns = timeout_ns
     if form:
         (g.form.kind, g.form.bias, g.form.act, g.form.round, g.form.scale, g.form.residual) = form
-    _check("b200k_gemm_epilogue", library().b200k_gemm_epilogue(ctypes.byref(g), _stream()))
+    if noalloc:
+        _check("b200k_gemm_epilogue_noalloc", library().b200k_gemm_epilogue_noalloc(ctypes.byref(g), _stream()))
+    else:
+        _check("b200k_gemm_epilogue", library().b200k_gemm_epilogue(ctypes.byref(g), _stream()))
 
 
 def rownorm(x: torch.Tensor, kind: int, weight, bias, eps: float, flags: int, out: torch.Tensor,

@@ -1046,3 +1046,37 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (cfg == 0) return launch_cfg<256, 4>(fast, bnm, ob, ta, tb, to, p, grid, st);
   return launch_cfg<128, 6>(fast, bnm, ob, ta, tb, to, p, grid, st);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry (see b200k.h): the status word lives in this
+// file-scope array instead of caller memory.  In host code the name below is
+// only a host-side stand-in; the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) int32_t g_noalloc_scratch[B200K_NOALLOC_SCRATCH_BYTES / sizeof(int32_t)];
+
+extern "C" int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream_) {
+  if (!args) return B200K_ERR_ARG;
+  const size_t need = B200K_NOALLOC_STATUS_BYTES;  // one status word per call
+  if (need > sizeof(g_noalloc_scratch)) return B200K_ERR_SHAPE;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return B200K_ERR_DEVICE;
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  if (dev >= 64) return B200K_ERR_DEVICE;
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (addr[dev] == nullptr) {
+      void* p = nullptr;
+      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return B200K_ERR_LAUNCH;
+      addr[dev] = p;
+    }
+    scratch = addr[dev];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (cudaMemsetAsync(scratch, 0, need, st) != cudaSuccess) return B200K_ERR_LAUNCH;
+  B200kGemmArgs a = *args;
+  a.status = static_cast<int32_t*>(scratch);
+  return b200k_gemm_epilogue(&a, stream_);
+}
