@@ -51,6 +51,7 @@ def _use_reference_triton() -> None:
         raise RuntimeError("reference not installed in baseline/_ref")
     sys.path.insert(0, p)
 
+
 SWEEP = [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 14336)]
 ACTS = ["none", "gelu", "silu"]
 DOMINANT = (16384, 4096, 14336)
@@ -97,9 +98,12 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)  # the timed region starts once sampling runs
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -411,13 +415,17 @@ def run_single_gemm(args, dist: Dist) -> dict:
     torch.cuda.synchronize()
     wall_us = (time.perf_counter() - t0) / 50 * 1e6
     ms = statistics.median(times)
+    # the same block in eager PyTorch (cuBLAS addmm + ATen epilogue kernels)
+    with torch.no_grad():
+        eager_ms = statistics.median(_time_device(lambda: blk(x, r), args.steps, args.warmup, flush))
     return {"metric": "fused GEMM+epilogue TFLOP/s", "value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": "gemm_epilogue", "M": M, "N": N, "K": K, "act": args.act,
                        "tile_config": args.tile_config, "program_len": len(code),
                        "epilogue_path": "compiled" if form else "interpreted"},
-            "back_to_back_us_per_call": round(wall_us, 1)}
+            "back_to_back_us_per_call": round(wall_us, 1),
+            "eager_ms": round(eager_ms, 4), "eager_tflops": round(2.0 * M * N * K / (eager_ms * 1e-3) / 1e12, 1)}
 
 
 def _backend(name: str):
