@@ -208,7 +208,17 @@ typedef struct {
   int64_t timeout_ns;  /* 0 = default (2 s) */
   B200kEpilogueForm form;
   int32_t pad2;
+  /* Optional diagnostic timeline (NULL = off): per CTA, B200K_GEMM_TRACE_WORDS
+   * global-timer stamps (ns) -- [0] entry, [1] set-up done, [2] exit, then per
+   * tile i < 40 at 8 + 6*i: first and last TMA issue, MMA start, last MMA
+   * commit, epilogue start, epilogue end; for the first tile, words 248..255
+   * hold per 32-column sub-chunk (s < 4) the time the accumulator was read
+   * and the time the staging buffer was free.  Ignored unless trace_words covers
+   * every CTA (148 x B200K_GEMM_TRACE_WORDS on a B200). */
+  uint64_t* trace;
+  int64_t trace_words;
 } B200kGemmArgs;
+#define B200K_GEMM_TRACE_WORDS 256
 
 int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 

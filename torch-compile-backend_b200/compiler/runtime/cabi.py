@@ -70,7 +70,9 @@ class GemmArgs(ctypes.Structure):
                 ("n_extras", ctypes.c_int32), ("tile_config", ctypes.c_int32),
                 ("extras", EpiOperand * (MAX_INPUTS - 1)), ("program", Program),
                 ("status", ctypes.c_void_p), ("timeout_ns", ctypes.c_int64), ("form", EpilogueForm),
-                ("pad2", ctypes.c_int32)]
+                ("pad2", ctypes.c_int32), ("trace", ctypes.c_void_p), ("trace_words", ctypes.c_int64)]
+
+TRACE_WORDS = 256
 
 
 class RowNormArgs(ctypes.Structure):
@@ -165,7 +167,7 @@ def pointwise(inputs: list[torch.Tensor], code, imm, out: torch.Tensor) -> None:
 
 def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], code, imm, out: torch.Tensor,
                   tile_config: int = -1, status: torch.Tensor | None = None, timeout_ns: int = 0,
-                  form=None, noalloc: bool = False) -> None:
+                  form=None, noalloc: bool = False, trace: torch.Tensor | None = None) -> None:
     """out[M,N] = program(a @ b, extras) with extras given as [M,N]-broadcastable tensors.
     noalloc=True calls b200k_gemm_epilogue_noalloc, which ignores `status` and
     uses the library's own status scratch (for hosts that cannot allocate)."""
@@ -191,6 +193,8 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
     g.timeout_ns = timeout_ns
     if form:
         (g.form.kind, g.form.bias, g.form.act, g.form.round, g.form.scale, g.form.residual) = form
+    if trace is not None:  # int64 device tensor, TRACE_WORDS per CTA
+        g.trace, g.trace_words = trace.data_ptr(), trace.numel()
     if noalloc:
         _check("b200k_gemm_epilogue_noalloc", library().b200k_gemm_epilogue_noalloc(ctypes.byref(g), _stream()))
     else:

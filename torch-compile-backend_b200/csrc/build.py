@@ -30,8 +30,9 @@ INCLUDE = os.path.join(REPO, "include")
 OUT_DIR = os.path.join(PKG, "compiler", "runtime")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-CU_SOURCES = ["capi.cu", "pointwise.cu", "rowreduce.cu", "gemm_sm100.cu"]
-HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h")] + [os.path.join(INCLUDE, "b200k.h")]
+CU_SOURCES = ["capi.cu", "pointwise.cu", "rowreduce.cu", "gemm_sm100.cu", "gemm_fast_bn256.cu", "gemm_fast_bn128.cu"]
+HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h", "gemm_kernel.cuh")] + [
+    os.path.join(INCLUDE, "b200k.h")]
 LIB = os.path.join(OUT_DIR, "libb200k.so")
 EXT = os.path.join(OUT_DIR, "_b200_ops.so")
 
