@@ -169,6 +169,62 @@ def test_gemm_edge_shapes(M, N, K, config, ab, path):
     _assert_close(out, want, *_gemm_tol(want))
 
 
+def role_program(act: str, role: str, round_to: str | None):
+    """Program for out = [round(] act(acc + bias) [)] (+ m | * m) with extras
+    (bias, m): the rounding cast, when given, sits where the decomposed graph
+    of a 16-bit model has it, between the activation and the 16-bit op."""
+    spec = [list(s) for s in ACTS[act]]
+    last = ["node", len(spec) - 1] if spec else ["acc"]
+    if round_to is not None:
+        spec.append(["_to_copy.default", [last, round_to]])
+        last = ["node", len(spec) - 1]
+    spec.append(["add.Tensor" if role == "res" else "mul.Tensor", [last, ["in", 1]]])
+    nodes, ops = spec_graph.build(spec, 2, with_acc=True)
+    prog = compile_group(nodes, ops, prologue=[("ADD", ops[1])], prologue_target=ops[0], rounding_casts=True)
+    return prog.code, prog.imm, spec, canonical_form(prog, 3)
+
+
+@pytest.mark.parametrize("role", ["res", "scale"])
+@pytest.mark.parametrize("act", ["none", "silu", "gelu"])
+@pytest.mark.parametrize("dt", ["bfloat16", "float16"])
+@pytest.mark.parametrize("rounded", [True, False])
+@pytest.mark.parametrize("config", [0, 1])
+def test_gemm_row_operand_roles(role, act, dt, rounded, config):
+    """A full 16-bit matrix as residual or scale, after an activation that is
+    (rounded) or is not rounded to the output type first.  Rounded, the
+    compiled path applies the op to packed 16-bit pairs; the result equals
+    the interpreted program's bit for bit where both paths share the
+    activation's implementation (none, silu) and the fp32 oracle within the
+    GEMM tolerance everywhere.  Ragged M and N cover partial tiles."""
+    M, N, K = 300, 520, 200
+    t = _tdt(dt)
+    g = torch.Generator(device=DEV).manual_seed(11)
+    x = torch.randn(M, K, device=DEV, generator=g).to(t)
+    w = (0.1 * torch.randn(N, K, device=DEV, generator=g)).to(t)
+    b = torch.randn(N, device=DEV, generator=g).to(t)
+    m = torch.randn(M, N, device=DEV, generator=g).to(t)
+    code, imm, spec, form = role_program(act, role, dt if rounded else None)
+    assert form is not None and form[3] == (B200K_DT[dt] if rounded else -1)
+    assert form[5 if role == "res" else 4] == 1
+    outs = {}
+    for path in ("compiled", "interpreted"):
+        out = torch.empty(M, N, device=DEV, dtype=t)
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        cabi.gemm_epilogue(x, w.t(), [b, m], code, imm, out, tile_config=config, status=status,
+                           form=form if path == "compiled" else None)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        outs[path] = out
+    if act != "gelu":
+        assert torch.equal(outs["compiled"], outs["interpreted"])
+    want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), m.float().cpu().numpy()], dt, bias=b.float().cpu().numpy())
+    _assert_close(outs["compiled"], want, *_gemm_tol(want))
+
+
+B200K_DT = {"float32": 0, "float16": 1, "bfloat16": 2}
+
+
 @pytest.mark.parametrize("out_dtype", ["float32", "float16"])
 def test_gemm_extras_broadcast_and_strided(out_dtype):
     """Epilogue operands of every layout: [M,1] column, 0-d scalar, fp32 row

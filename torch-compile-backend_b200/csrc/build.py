@@ -30,7 +30,12 @@ INCLUDE = os.path.join(REPO, "include")
 OUT_DIR = os.path.join(PKG, "compiler", "runtime")
 BUILD_DIR = os.path.join(PKG, "_build")
 
-CU_SOURCES = ["capi.cu", "pointwise.cu", "rowreduce.cu", "gemm_sm100.cu", "gemm_fast_bn256.cu", "gemm_fast_bn128.cu"]
+# (source, object name, defines).  gemm_fast.cu is compiled once per
+# (tile width, activation) pair that has compiled-epilogue kernels; the
+# activations are B200K_ACT_NONE, GELU_ERF, GELU_TANH, SILU, RELU.
+CU_UNITS = [(src, os.path.splitext(src)[0], []) for src in ("capi.cu", "pointwise.cu", "rowreduce.cu", "gemm_sm100.cu")]
+CU_UNITS += [("gemm_fast.cu", f"gemm_fast_{bn}_{act}", [f"-DB200K_FAST_BN={bn}", f"-DB200K_FAST_ACT={act}"])
+             for bn in (256, 128) for act in (0, 1, 2, 3, 4)]
 HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h", "gemm_kernel.cuh")] + [
     os.path.join(INCLUDE, "b200k.h")]
 LIB = os.path.join(OUT_DIR, "libb200k.so")
@@ -57,11 +62,12 @@ def _run(cmd: list[str], verbose: bool) -> None:
         raise RuntimeError(f"build step failed: {' '.join(cmd[:3])} ...")
 
 
-def _compile_cu(src: str, force: bool, verbose: bool) -> str:
-    obj = os.path.join(BUILD_DIR, os.path.splitext(src)[0] + ".o")
+def _compile_cu(unit: tuple[str, str, list[str]], force: bool, verbose: bool) -> str:
+    src, name, defines = unit
+    obj = os.path.join(BUILD_DIR, name + ".o")
     path = os.path.join(HERE, src)
     if force or _newer(obj, [path] + HEADERS):
-        _run([NVCC] + NVCC_FLAGS + ["-c", path, "-o", obj], verbose)
+        _run([NVCC] + NVCC_FLAGS + defines + ["-c", path, "-o", obj], verbose)
     return obj
 
 
@@ -84,8 +90,8 @@ def build(force: bool = False, verbose: bool = False) -> tuple[str, str]:
     os.makedirs(BUILD_DIR, exist_ok=True)
     os.makedirs(OUT_DIR, exist_ok=True)
     ext_src = os.path.join(HERE, "torch_ops.cpp")
-    with cf.ThreadPoolExecutor(max_workers=len(CU_SOURCES)) as pool:
-        objs = list(pool.map(lambda s: _compile_cu(s, force, verbose), CU_SOURCES))
+    with cf.ThreadPoolExecutor(max_workers=min(len(CU_UNITS), os.cpu_count() or 4)) as pool:
+        objs = list(pool.map(lambda u: _compile_cu(u, force, verbose), CU_UNITS))
         if force or _newer(LIB, objs):
             _run([NVCC] + ARCH_FLAGS + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs, verbose)
         if force or _newer(EXT, [ext_src, LIB, os.path.join(INCLUDE, "b200k.h")]):

@@ -1,0 +1,51 @@
+// Compiled-epilogue GEMM kernels for one (tile width, activation) pair.  The
+// build compiles this file once per pair, defining B200K_FAST_BN (256 or 128)
+// and B200K_FAST_ACT (a B200K_ACT_* value), so the instantiations compile in
+// parallel.  Each object defines launch_fast_<BN>_<ACT>, which covers K-major
+// B with 16-bit output and every row role, N-major B with 16-bit output and
+// every row role, and K-major B with fp32 output without a row operand.
+#include "gemm_kernel.cuh"
+
+#if !defined(B200K_FAST_BN) || !defined(B200K_FAST_ACT)
+#error "compile with -DB200K_FAST_BN=<256|128> -DB200K_FAST_ACT=<activation>"
+#endif
+
+namespace b200k {
+namespace gemm {
+namespace {
+
+constexpr int kBN = B200K_FAST_BN;
+constexpr int kStages = kBN == 256 ? kConfigs[0].stages : kConfigs[1].stages;
+constexpr int kAct = B200K_FAST_ACT;
+static_assert((kBN == 256 && kConfigs[0].bn == 256) || (kBN == 128 && kConfigs[1].bn == 128), "tile configs");
+
+template <bool BNM>
+int launch_row16(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p,
+                 int grid, cudaStream_t st) {
+  switch (row) {
+    case ROW_NONE: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_NONE>(ta, tb, to, p, grid, st);
+    case ROW_SCALE: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_SCALE>(ta, tb, to, p, grid, st);
+    case ROW_RES: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_RES>(ta, tb, to, p, grid, st);
+    case ROW_SCALE_PK: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_SCALE_PK>(ta, tb, to, p, grid, st);
+    case ROW_RES_PK: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_RES_PK>(ta, tb, to, p, grid, st);
+    default: return B200K_ERR_UNSUPPORTED;
+  }
+}
+
+}  // namespace
+
+#define B200K_FAST_FN2(BN, ACT) launch_fast_##BN##_##ACT
+#define B200K_FAST_FN(BN, ACT) B200K_FAST_FN2(BN, ACT)
+
+int B200K_FAST_FN(B200K_FAST_BN, B200K_FAST_ACT)(bool bnm, int ob, int row, const CUtensorMap& ta,
+                                                 const CUtensorMap& tb, const CUtensorMap& to, const Params& p,
+                                                 int grid, cudaStream_t st) {
+  if (ob == 2) return bnm ? launch_row16<true>(row, ta, tb, to, p, grid, st)
+                          : launch_row16<false>(row, ta, tb, to, p, grid, st);
+  if (ob == 4 && !bnm && row == ROW_NONE)
+    return launch_one<kBN, kStages, false, 4, true, kAct, ROW_NONE>(ta, tb, to, p, grid, st);
+  return B200K_ERR_UNSUPPORTED;
+}
+
+}  // namespace gemm
+}  // namespace b200k

@@ -75,6 +75,7 @@ struct Params {
   uint32_t idesc;
   int32_t f_bias, f_act, f_round, f_scale, f_res;  // canonical epilogue form (fast path)
   int32_t xm_bias, xm_scale, xm_res;               // how the fast path stages each operand (XM_*)
+  int32_t row_idx;                                 // extras index of the fast path's full-matrix operand
   int32_t pad2;
   unsigned long long* trace;                       // diagnostic timeline, null = off
   EpiOperand ex[B200K_MAX_INPUTS - 1];
@@ -95,14 +96,18 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// The waiting thread is suspended until the phase completes or, at the
+// latest, after kSuspendNs; the hint keeps waiting warps from spinning and
+// taking issue slots from the epilogue warps on the same scheduler.
+constexpr uint32_t kSuspendNs = 1000000;
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}\n"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(kSuspendNs)
       : "memory");
   return ok != 0;
 }
@@ -177,15 +182,13 @@ struct Ctl {
 __device__ __forceinline__ bool wait_bar(uint64_t* bar, uint32_t parity, const Ctl& c) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 15u) == 0) {
-      if (*c.abort) return false;
-      if (global_timer_ns() - t0 > c.timeout_ns) {
-        *c.abort = 1;
-        if (c.status) atomicCAS(c.status, 0, B200K_ERR_TIMEOUT);
-        return false;
-      }
+    if (*c.abort) return false;
+    if (global_timer_ns() - t0 > c.timeout_ns) {
+      *c.abort = 1;
+      if (c.status) atomicCAS(c.status, 0, B200K_ERR_TIMEOUT);
+      return false;
     }
   }
 }
@@ -339,18 +342,61 @@ __device__ __forceinline__ void epilogue_group(const Params& p, uint32_t taddr, 
 // ------------------------------------------------------- canonical fast path
 // v = acc; v += E[bias]; v = act(v); v = round(v); v *= E[scale]; v += E[res]
 // with the same fp32 operation order as the decomposed ATen graph it replaces.
+__device__ __forceinline__ float approx_rcp(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float approx_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// GELU(x) = x/2 (1 + erf(x / sqrt 2)) through the complementary error
+// function of Abramowitz & Stegun, Handbook of Mathematical Functions,
+// eq. 7.1.26: for y >= 0, erfc(y) = t (a1 + t (a2 + t (a3 + t (a4 + t a5))))
+// exp(-y^2) + e(y), t = 1 / (1 + p y), |e(y)| <= 1.5e-7.  With y = |x|/sqrt 2
+// and r = 1/2 - erfc(y)/2, GELU = x/2 + |x| r for either sign of x.  The
+// coefficients below are a1..a5 halved and p / sqrt 2; exp(-y^2) =
+// 2^(-x^2 log2(e) / 2).  Absolute error of the result is below
+// 1e-7 (1 + |x|) plus the hardware rcp/ex2 rounding; +inf maps to +inf and
+// NaN / -inf to NaN as in the erf formula.  Written stage by stage over the
+// eight values so the independent chains interleave.
+__device__ __forceinline__ void gelu_erf_as8(float (&v)[8]) {
+  float t[8], e[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) t[j] = approx_rcp(fmaf(0.2316418882663604f, fabsf(v[j]), 1.0f));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) e[j] = approx_exp2((v[j] * -0.72134752044448170f) * v[j]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    float q = fmaf(0.5307027145f, t[j], -0.7265760135f);
+    q = fmaf(q, t[j], 0.7107068705f);
+    q = fmaf(q, t[j], -0.142248368f);
+    q = fmaf(q, t[j], 0.127414796f);
+    const float r = fmaf(-(q * t[j]), e[j], 0.5f);
+    v[j] = fmaf(fabsf(v[j]), r, 0.5f * v[j]);
+  }
+}
+
+// Separate ops of the decomposed graph (bias add, the activation's final
+// multiply, the scale / residual op) use __fadd_rn / __fmul_rn so the compiler
+// never contracts two of them into one rounding, as eager execution would not.
 template <int ACT>
 __device__ __forceinline__ void apply_act8(float (&v)[8]) {
+  if constexpr (ACT == B200K_ACT_GELU_ERF) {
+    gelu_erf_as8(v);
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float x = v[j];
-    if constexpr (ACT == B200K_ACT_GELU_ERF) {
-      v[j] = (x * 0.5f) * (erff(x * 0.7071067811865476f) + 1.0f);
-    } else if constexpr (ACT == B200K_ACT_GELU_TANH) {
+    if constexpr (ACT == B200K_ACT_GELU_TANH) {
       const float t3 = x + ((x * x) * x) * 0.044715f;
       v[j] = (x * 0.5f) * (op_tanh(t3 * 0.7978845608028654f) + 1.0f);
     } else if constexpr (ACT == B200K_ACT_SILU) {
-      v[j] = x * op_sigmoid(x);
+      v[j] = __fmul_rn(x, op_sigmoid(x));
     } else if constexpr (ACT == B200K_ACT_RELU) {
       v[j] = fmaxf(x, 0.0f);
     } else if constexpr (ACT == B200K_ACT_SIGMOID) {
@@ -363,21 +409,37 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
 
 // ------------------------------------------- fast path, latency-hiding loop
 // Operand staging modes, chosen on the host per operand:
-//   XM_BCAST   row-broadcast vector (stride_m == 0, e.g. a bias): each lane
-//              loads one column of the 32-column sub-chunk (one coalesced
-//              load per warp) and the values reach every row by __shfl_sync;
+//   XM_BCAST   row-broadcast f32/bf16/f16 vector (stride_m == 0, e.g. a
+//              bias): each lane loads one column of the 32-column sub-chunk
+//              (one coalesced load per warp) and the values reach every row
+//              by __shfl_sync;
 //   XM_ROW16   full 16-bit matrix with unit column stride (a residual, or the
 //              `up` operand of SwiGLU): each lane loads its own row's 32
 //              values (64 bytes) into registers;
 //   XM_GENERIC anything else -- such programs run on the interpreter kernel.
-// At most one operand is XM_ROW16.  Operands are prefetched one 32-column
-// sub-chunk ahead, across tile boundaries, into one of two register sets
-// that alternate between statically named copies.
+// The compiled path takes a bias in XM_BCAST and at most one of scale and
+// residual, in XM_ROW16 (its role is the kernel's ROW parameter, below).
+// Operands are loaded one 32-column sub-chunk ahead, across tile boundaries,
+// into a second register set that becomes the current one when the
+// sub-chunk is done.  The sub-chunk body exists once in the code and
+// edge-of-matrix loads are out of line, which keeps the epilogue warps' hot
+// loop small enough for the instruction cache.
 enum { XM_NONE = 0, XM_BCAST = 1, XM_ROW16 = 2, XM_GENERIC = 3 };
 
+// Role of the full-matrix operand in a compiled epilogue:
+//   ROW_NONE     no scale, no residual;
+//   ROW_SCALE    v * s and ROW_RES  v + r in fp32, rounded once by the store;
+//   ROW_SCALE_PK / ROW_RES_PK: the form rounds the activation to the output
+//                type and s / r has that type, so the multiply / add runs on
+//                packed bf16x2 / f16x2 pairs.  A product or sum of two values
+//                of an 8- or 11-bit-significand type is exact in fp32, so the
+//                packed op's single rounding equals fp32-then-round, the
+//                decomposed graph's order.
+enum { ROW_NONE = 0, ROW_SCALE = 1, ROW_RES = 2, ROW_SCALE_PK = 3, ROW_RES_PK = 4 };
+
 struct FastOps {
-  float bias_b, scale_b, res_b;
-  uint4 row_r[4];  // the XM_ROW16 operand (scale or residual)
+  float bias_b;
+  uint4 row_r[4];  // the full-matrix operand's 32 values of this lane's row
 };
 
 // 32 lanes x 32 bit, 32 consecutive columns.
@@ -393,163 +455,190 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// Lane l's column n + l of a row-broadcast operand (f32, bf16 or f16).
 __device__ __forceinline__ float load_bcast(const EpiOperand& e, int n, int lane, int N) {
   const int col = n + lane;
-  return col < N ? load_scalar(e.ptr, static_cast<int64_t>(col) * e.sn, e.dt) : 0.0f;
+  if (col >= N) return 0.0f;
+  const int64_t off = static_cast<int64_t>(col) * e.sn;
+  if (e.dt == B200K_F32) return __ldg(reinterpret_cast<const float*>(e.ptr) + off);
+  const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(e.ptr) + off);
+  return e.dt == B200K_BF16 ? __uint_as_float(static_cast<uint32_t>(u) << 16) : __half2float(__ushort_as_half(u));
+}
+
+// Eight 16-bit values of one row from column n, zero at and beyond column N.
+static __device__ __noinline__ uint4 load_row16_edge8(const uint16_t* row, int n, int N) {
+  uint32_t w[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t lo = n + 2 * j < N ? row[n + 2 * j] : 0u;
+    const uint32_t hi = n + 2 * j + 1 < N ? row[n + 2 * j + 1] : 0u;
+    w[j] = lo | (hi << 16);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
 __device__ __forceinline__ void load_row16(const EpiOperand& e, int m, int n, int M, int N, uint4 (&b)[4]) {
-  const uint16_t* base = reinterpret_cast<const uint16_t*>(e.ptr);
+  const uint16_t* row = reinterpret_cast<const uint16_t*>(e.ptr) + static_cast<int64_t>(m) * e.sm;
   if (m < M && n + 32 <= N) {
-    const uint4* q = reinterpret_cast<const uint4*>(base + static_cast<int64_t>(m) * e.sm + n);
+    const uint4* q = reinterpret_cast<const uint4*>(row + n);
 #pragma unroll
     for (int i = 0; i < 4; ++i) b[i] = __ldg(q + i);
+  } else if (m < M) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) b[i] = load_row16_edge8(row, n + 8 * i, N);
   } else {
-    uint32_t w[16];
 #pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      const uint32_t lo = (m < M && n + 2 * j < N) ? base[static_cast<int64_t>(m) * e.sm + n + 2 * j] : 0u;
-      const uint32_t hi = (m < M && n + 2 * j + 1 < N) ? base[static_cast<int64_t>(m) * e.sm + n + 2 * j + 1] : 0u;
-      w[j] = lo | (hi << 16);
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) b[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+    for (int i = 0; i < 4; ++i) b[i] = make_uint4(0u, 0u, 0u, 0u);
   }
 }
 
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+
+// Warms L2 with this lane's row of the full-matrix operand (residual or
+// scale) for the tile at (m, n): the warp's BN/2 columns, which the
+// sub-chunks later read straight into registers.  Issued one tile ahead, so
+// those reads wait on L2 rather than DRAM.
+template <int BN, int ROW>
+__device__ __forceinline__ void prefetch_row16_l2(const Params& p, int m, int n) {
+  if (ROW == ROW_NONE || m >= p.M || n >= p.N) return;
+  const EpiOperand& e = p.ex[p.row_idx];
+  const int bytes = min(BN / 2, p.N - n) * 2;
+  const char* row = reinterpret_cast<const char*>(e.ptr) + (static_cast<int64_t>(m) * e.sm + n) * 2;
+  for (int off = 0; off < bytes; off += 128) prefetch_l2(row + off);
+  prefetch_l2(row + bytes - 1);  // the line of the last byte when the row is not 128-byte aligned
+}
+
+template <int ROW>
 __device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, int lane, FastOps& f) {
-  if (p.xm_bias == XM_BCAST) f.bias_b = load_bcast(p.ex[p.f_bias], n, lane, p.N);
-  if (p.xm_scale == XM_BCAST) f.scale_b = load_bcast(p.ex[p.f_scale], n, lane, p.N);
-  else if (p.xm_scale == XM_ROW16) load_row16(p.ex[p.f_scale], m, n, p.M, p.N, f.row_r);
-  if (p.xm_res == XM_BCAST) f.res_b = load_bcast(p.ex[p.f_res], n, lane, p.N);
-  else if (p.xm_res == XM_ROW16) load_row16(p.ex[p.f_res], m, n, p.M, p.N, f.row_r);
+  if (p.f_bias >= 0) f.bias_b = load_bcast(p.ex[p.f_bias], n, lane, p.N);
+  if constexpr (ROW != ROW_NONE) load_row16(p.ex[p.row_idx], m, n, p.M, p.N, f.row_r);
+}
+
+__device__ __forceinline__ uint32_t pk_op(uint32_t a, uint32_t b, bool bf16, bool mul) {
+  uint32_t d;
+  if (bf16) {
+    if (mul) asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    else asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  } else {
+    if (mul) asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    else asm("add.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  }
+  return d;
 }
 
 __device__ __forceinline__ void unpack16x8(uint4 u, int dt, float (&x)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+  if (dt == B200K_BF16) {
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    float2 f;
-    if (dt == B200K_BF16) f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-    else f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
-    x[2 * j] = f.x;
-    x[2 * j + 1] = f.y;
-  }
-}
-
-// The operand of one role for columns [n_g, n_g + 8) of the current sub-chunk (group g).
-__device__ __forceinline__ void operand8(const Params& p, int mode, int idx, float bval, const uint4 (&r)[4], int g,
-                                         float (&x)[8]) {
-  if (mode == XM_BCAST) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[j] = __shfl_sync(0xffffffffu, bval, g * 8 + j);
+    for (int j = 0; j < 4; ++j) {
+      x[2 * j] = __uint_as_float(w[j] << 16);
+      x[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    }
   } else {
-    unpack16x8(r[g], p.ex[idx].dt, x);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      x[2 * j] = f.x;
+      x[2 * j + 1] = f.y;
+    }
   }
 }
 
-// One 32-column sub-chunk of one output row per lane: prefetch the operands
-// of the next sub-chunk into `fill`, read the accumulator from TMEM, apply
-// the canonical epilogue with the operands already in `use`, stage, store.
-// `use` and `fill` are distinct named register sets at every call site, so
-// reading `use` never waits on the loads just issued into `fill`.
-template <int BN, int OUT_BYTES, int ACT>
-__device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, uint32_t t_row, int t,
-                                               int tm, int tn, int s, int quarter, int half, int lane, uint8_t* sb,
-                                               const FastOps& use, FastOps& fill, bool stamp_subs) {
+// One 32-column sub-chunk of one output row per lane (columns n..n+31 of
+// row m, TMEM columns t_col..t_col+31): read the accumulator, apply the
+// canonical epilogue with the operands in `use`, stage, and store every
+// 128-byte staging row with one TMA store per warp.
+template <int BN, int OUT_BYTES, int ACT, int ROW>
+__device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, uint32_t t_col, int row0,
+                                               int n, int s, int lane, uint8_t* sb, const FastOps& use,
+                                               bool stamp_subs) {
   constexpr int kEC = 128 / OUT_BYTES;
   constexpr int NSUB = (BN / 2) / 32;
   constexpr int SUB_PER_STG = kEC / 32;
-  const int m = tm * BM + quarter * 32 + lane;
-  const int n = tn * BN + half * (BN / 2) + s * 32;
-  if (s + 1 < NSUB) {
-    fast_prefetch(p, m, n + 32, lane, fill);
-  } else if (t + static_cast<int>(gridDim.x) < p.num_tiles) {
-    int tm2, tn2;
-    tile_coords(t + gridDim.x, p, tm2, tn2);
-    fast_prefetch(p, tm2 * BM + quarter * 32 + lane, tn2 * BN + half * (BN / 2), lane, fill);
-  }
-  if (n >= p.N) return;  // warp-uniform
+  constexpr bool kPacked = ROW == ROW_SCALE_PK || ROW == ROW_RES_PK;
+  constexpr bool kMul = ROW == ROW_SCALE || ROW == ROW_SCALE_PK;
+  static_assert(OUT_BYTES == 2 || ROW == ROW_NONE, "full-matrix operands are 16-bit, as is the output");
   uint32_t raw[32];
-  tmem_ld32(t_row + s * 32, raw);
+  tmem_ld32(t_col, raw);
   tmem_wait_ld();
-  // first tile of the trace: per sub-chunk, TMEM data in hand / staging free
   if (stamp_subs && s < 4) stamp(p, 248 + 2 * s);
   const int sub = s % SUB_PER_STG;
-  if (sub == 0 && !p.direct_store) {
+  if (sub == 0) {
     if (lane == 0) bulk_wait_read_all();
     __syncwarp();
   }
   if (stamp_subs && s < 4) stamp(p, 249 + 2 * s);
+  const bool out_bf16 = p.out_dt == B200K_BF16;
 #pragma unroll
   for (int g = 0; g < 4; ++g) {
-    const int ng = n + g * 8;
-    float v[8], x[8];
+    float v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[g * 8 + j]);
     if (p.f_bias >= 0) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] += __shfl_sync(0xffffffffu, use.bias_b, g * 8 + j);
+      for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(0xffffffffu, use.bias_b, g * 8 + j));
     }
     apply_act8<ACT>(v);
-    if (p.f_round == B200K_BF16) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
-    } else if (p.f_round == B200K_F16) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
-    }
-    if (p.f_scale >= 0) {
-      operand8(p, p.xm_scale, p.f_scale, use.scale_b, use.row_r, g, x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] *= x[j];
-    }
-    if (p.f_res >= 0) {
-      operand8(p, p.xm_res, p.f_res, use.res_b, use.row_r, g, x);
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] += x[j];
-    }
-    if (p.direct_store) {
-      if (m < p.M) {
-        const int64_t off = static_cast<int64_t>(m) * p.out_sm + ng;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (ng + j < p.N) store_scalar(p.out, off + j, p.out_dt, v[j]);
-      }
-    } else if (OUT_BYTES == 2) {
-      const uint4 u = (p.out_dt == B200K_BF16) ? pack_bf16x8(v) : pack_f16x8(v);
+    if constexpr (kPacked) {
+      uint4 u = out_bf16 ? pack_bf16x8(v) : pack_f16x8(v);
+      const uint4 r = use.row_r[g];
+      u.x = pk_op(u.x, r.x, out_bf16, kMul);
+      u.y = pk_op(u.y, r.y, out_bf16, kMul);
+      u.z = pk_op(u.z, r.z, out_bf16, kMul);
+      u.w = pk_op(u.w, r.w, out_bf16, kMul);
       const int chunk = sub * 4 + g;
       *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u;
     } else {
+      if (p.f_round == B200K_BF16) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int chunk = 2 * g + h;
-        *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
-            make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+        for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
+      } else if (p.f_round == B200K_F16) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
+      }
+      if constexpr (ROW != ROW_NONE) {
+        float x[8];
+        unpack16x8(use.row_r[g], out_bf16 ? B200K_BF16 : B200K_F16, x);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] = kMul ? __fmul_rn(v[j], x[j]) : __fadd_rn(v[j], x[j]);
+      }
+      if constexpr (OUT_BYTES == 2) {
+        const uint4 u = out_bf16 ? pack_bf16x8(v) : pack_f16x8(v);
+        const int chunk = sub * 4 + g;
+        *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u;
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int chunk = 2 * g + h;
+          *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
+              make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
+        }
       }
     }
   }
-  if (!p.direct_store && (sub == SUB_PER_STG - 1 || s + 1 == NSUB || n + 32 >= p.N)) {
+  if (sub == SUB_PER_STG - 1 || s + 1 == NSUB || n + 32 >= p.N) {
     fence_async_smem();
     __syncwarp();
     if (lane == 0) {
-      tma_store_2d(tmO, sb, n - sub * 32, tm * BM + quarter * 32);
+      tma_store_2d(tmO, sb, n - sub * 32, row0);
       bulk_commit();
     }
   }
 }
 
-template <int BN, int OUT_BYTES, int ACT>
+template <int BN, int OUT_BYTES, int ACT, int ROW>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
                                                    uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
                                                    int half, int lane, const Ctl& ctl) {
-  constexpr int NSUB = (BN / 2) / 32;  // 32-column sub-chunks per warp and tile (even)
-  static_assert(NSUB % 2 == 0, "sub-chunks alternate between two named register sets");
-  FastOps opa, opb;
+  constexpr int NSUB = (BN / 2) / 32;  // 32-column sub-chunks per warp and tile
+  FastOps cur{}, nxt{};
   if (static_cast<int>(blockIdx.x) < p.num_tiles) {
     int tm, tn;
     tile_coords(blockIdx.x, p, tm, tn);
-    fast_prefetch(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2), lane, opa);
+    prefetch_row16_l2<BN, ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2));
+    fast_prefetch<ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2), lane, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
@@ -558,17 +647,31 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++ti) {
     int tm, tn;
     tile_coords(t, p, tm, tn);
+    const bool more = t + static_cast<int>(gridDim.x) < p.num_tiles;
+    int m2 = 0, n2 = 0;
+    if (more) {
+      int tm2, tn2;
+      tile_coords(t + gridDim.x, p, tm2, tn2);
+      m2 = tm2 * BM + quarter * 32 + lane;
+      n2 = tn2 * BN + half * (BN / 2);
+      prefetch_row16_l2<BN, ROW>(p, m2, n2);
+    }
     if (!wait_bar(&tfull[acc], aph, ctl)) break;
     tc_fence_after();
     if (stamper) stamp_tile(p, ti, 4);
+    const int row0 = tm * BM + quarter * 32;
+    const int m = row0 + lane;
+    const int n0 = tn * BN + half * (BN / 2);
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                            static_cast<uint32_t>(acc * BN + half * (BN / 2));
 #pragma unroll 1
-    for (int s = 0; s < NSUB; s += 2) {
-      fast_sub_chunk<BN, OUT_BYTES, ACT>(p, tmO, t_row, t, tm, tn, s, quarter, half, lane, sb, opa, opb,
-                                         stamper && ti == 0);
-      fast_sub_chunk<BN, OUT_BYTES, ACT>(p, tmO, t_row, t, tm, tn, s + 1, quarter, half, lane, sb, opb, opa,
-                                         stamper && ti == 0);
+    for (int s = 0; s < NSUB; ++s) {
+      const int n = n0 + s * 32;
+      if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, lane, nxt);
+      else if (more) fast_prefetch<ROW>(p, m2, n2, lane, nxt);
+      if (n < p.N)  // warp-uniform
+        fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur, stamper && ti == 0);
+      cur = nxt;
     }
     if (stamper) stamp_tile(p, ti, 5);
     tc_fence_before();
@@ -579,7 +682,7 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       aph ^= 1u;
     }
   }
-  if (!p.direct_store && lane == 0) bulk_wait_all();
+  if (lane == 0) bulk_wait_all();
   __syncwarp();
 }
 
@@ -596,7 +699,7 @@ struct Cfg {
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
 };
 
-template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT>
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
@@ -743,7 +846,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (FAST) {
     // ------------------------------------------------------------ epilogue (compiled form)
     const int ew = warp - 4;
-    epilogue_fast_loop<BN, OUT_BYTES, ACT>(p, &tmO, tmem_base, tfull, tempty, sStg + ew * kStgBytes, warp & 3,
+    epilogue_fast_loop<BN, OUT_BYTES, ACT, ROW>(p, &tmO, tmem_base, tfull, tempty, sStg + ew * kStgBytes, warp & 3,
                                            ew >> 2, lane, ctl);
     } else {
     // ------------------------------------------------------------ epilogue (interpreted program)
@@ -818,11 +921,11 @@ struct TileConfig {
 constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT>
+template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
                cudaStream_t st) {
   using C = Cfg<BN, STAGES, BNM, OB>;
-  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT>;
+  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT, ROW>;
   static bool attr_set = false;  // per instantiation; idempotent
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
@@ -833,14 +936,28 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
   return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
 }
 
-// Launchers of the compiled-epilogue kernels (one translation unit per tile
-// width so they compile in parallel); B200K_ERR_UNSUPPORTED for a combination
-// that has no compiled kernel (the caller then interprets the program).
-int launch_fast_bn256(int act, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                      const Params& p, int grid, cudaStream_t st);
-int launch_fast_bn128(int act, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                      const Params& p, int grid, cudaStream_t st);
-bool fast_combo_exists(int act, bool bnm, int ob);
+// Compiled-epilogue kernels exist for these activations (others interpret).
+constexpr int kFastActs[] = {B200K_ACT_NONE, B200K_ACT_GELU_ERF, B200K_ACT_GELU_TANH, B200K_ACT_SILU, B200K_ACT_RELU};
+
+// Launchers of the compiled-epilogue kernels, one translation unit per
+// (tile width, activation) so they compile in parallel (gemm_fast_*.cu).
+// Each covers K-major B with 16-bit output and every row role, N-major B
+// with 16-bit output and every row role, and K-major B with fp32 output
+// without a row operand; B200K_ERR_UNSUPPORTED for anything else.
+#define B200K_DECLARE_FAST(BN, ACT)                                                                          \
+  int launch_fast_##BN##_##ACT(bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb,     \
+                               const CUtensorMap& to, const Params& p, int grid, cudaStream_t st);
+B200K_DECLARE_FAST(256, 0)
+B200K_DECLARE_FAST(256, 1)
+B200K_DECLARE_FAST(256, 2)
+B200K_DECLARE_FAST(256, 3)
+B200K_DECLARE_FAST(256, 4)
+B200K_DECLARE_FAST(128, 0)
+B200K_DECLARE_FAST(128, 1)
+B200K_DECLARE_FAST(128, 2)
+B200K_DECLARE_FAST(128, 3)
+B200K_DECLARE_FAST(128, 4)
+#undef B200K_DECLARE_FAST
 
 }  // namespace gemm
 }  // namespace b200k

@@ -51,11 +51,29 @@ template <int BN, int STAGES>
 int launch_interp(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                   const Params& p, int grid, cudaStream_t st) {
   if (bnm) {
-    return ob == 2 ? launch_one<BN, STAGES, true, 2, false, -1>(ta, tb, to, p, grid, st)
-                   : launch_one<BN, STAGES, true, 4, false, -1>(ta, tb, to, p, grid, st);
+    return ob == 2 ? launch_one<BN, STAGES, true, 2, false, -1, ROW_NONE>(ta, tb, to, p, grid, st)
+                   : launch_one<BN, STAGES, true, 4, false, -1, ROW_NONE>(ta, tb, to, p, grid, st);
   }
-  return ob == 2 ? launch_one<BN, STAGES, false, 2, false, -1>(ta, tb, to, p, grid, st)
-                 : launch_one<BN, STAGES, false, 4, false, -1>(ta, tb, to, p, grid, st);
+  return ob == 2 ? launch_one<BN, STAGES, false, 2, false, -1, ROW_NONE>(ta, tb, to, p, grid, st)
+                 : launch_one<BN, STAGES, false, 4, false, -1, ROW_NONE>(ta, tb, to, p, grid, st);
+}
+
+int launch_fast(int bn, int act, bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb,
+                const CUtensorMap& to, const Params& p, int grid, cudaStream_t st) {
+#define B200K_FAST_CASE(BN, ACT) \
+  if (bn == BN && act == ACT) return launch_fast_##BN##_##ACT(bnm, ob, row, ta, tb, to, p, grid, st);
+  B200K_FAST_CASE(256, 0)
+  B200K_FAST_CASE(256, 1)
+  B200K_FAST_CASE(256, 2)
+  B200K_FAST_CASE(256, 3)
+  B200K_FAST_CASE(256, 4)
+  B200K_FAST_CASE(128, 0)
+  B200K_FAST_CASE(128, 1)
+  B200K_FAST_CASE(128, 2)
+  B200K_FAST_CASE(128, 3)
+  B200K_FAST_CASE(128, 4)
+#undef B200K_FAST_CASE
+  return B200K_ERR_UNSUPPORTED;
 }
 
 int pick(int64_t M, int64_t N, int sms) {
@@ -202,7 +220,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   auto mode_of = [&](int idx, bool allow_row) -> int32_t {
     if (idx < 0) return XM_NONE;
     const B200kEpiOperand& e = a->extras[idx];
-    if (e.stride_m == 0) return XM_BCAST;
+    const bool f_or_16 = e.dtype == B200K_F32 || e.dtype == B200K_BF16 || e.dtype == B200K_F16;
+    if (e.stride_m == 0) return f_or_16 ? XM_BCAST : XM_GENERIC;
     if (allow_row && e.stride_n == 1 && (e.dtype == B200K_BF16 || e.dtype == B200K_F16) && aligned16(e.ptr) &&
         e.stride_m % 8 == 0)
       return XM_ROW16;
@@ -230,14 +249,28 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (a->trace && a->trace_words >= static_cast<int64_t>(grid) * B200K_GEMM_TRACE_WORDS)
     p.trace = reinterpret_cast<unsigned long long*>(a->trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  // Compiled path: canonical form, no operand that needs the generic loader,
-  // at most one full-matrix operand, and a compiled kernel for this combination.
-  const bool fast = a->form.kind == 1 && p.xm_bias != XM_GENERIC && p.xm_bias != XM_ROW16 &&
-                    p.xm_scale != XM_GENERIC && p.xm_res != XM_GENERIC &&
-                    !(p.xm_scale == XM_ROW16 && p.xm_res == XM_ROW16) && fast_combo_exists(a->form.act, bnm, ob);
+  // Compiled path: canonical form, output storable by TMA, a row-broadcast
+  // bias (or none), at most one of scale and residual as a full 16-bit
+  // matrix of the output's type, and an activation with compiled kernels.
+  const int role_idx = a->form.residual >= 0 ? a->form.residual : a->form.scale;
+  const bool both = a->form.residual >= 0 && a->form.scale >= 0;
+  bool act_ok = false;
+  for (int fa : kFastActs) act_ok = act_ok || fa == a->form.act;
+  const bool row_ok = role_idx < 0 || (ob == 2 && mode_of(role_idx, true) == XM_ROW16 &&
+                                       a->extras[role_idx].dtype == a->out_dtype);
+  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
+                    (p.xm_bias == XM_NONE || p.xm_bias == XM_BCAST);
   if (fast) {
-    return cfg == 0 ? launch_fast_bn256(a->form.act, bnm, ob, ta, tb, to, p, grid, st)
-                    : launch_fast_bn128(a->form.act, bnm, ob, ta, tb, to, p, grid, st);
+    int row = ROW_NONE;
+    if (role_idx >= 0) {
+      const bool packed = a->form.round == a->out_dtype;  // round to the output type, then the 16-bit op
+      const bool res = a->form.residual >= 0;
+      row = res ? (packed ? ROW_RES_PK : ROW_RES) : (packed ? ROW_SCALE_PK : ROW_SCALE);
+      p.row_idx = role_idx;
+    } else if (a->form.round == a->out_dtype) {
+      p.f_round = -1;  // the store's own rounding is the same one
+    }
+    return launch_fast(bn, a->form.act, bnm, ob, row, ta, tb, to, p, grid, st);
   }
   if (cfg == 0) return launch_interp<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
   return launch_interp<128, 6>(bnm, ob, ta, tb, to, p, grid, st);
