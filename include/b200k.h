@@ -243,10 +243,13 @@ int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 #define B200K_NOALLOC_STATUS_BYTES 4
 int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream);
 
-/* Number of GEMM tile configurations in the built-in table and their shapes. */
+/* Number of GEMM tile configurations in the built-in table and their shapes.
+ * Config 2 (128 x 192 tiles) runs compiled epilogues only: a call forcing it
+ * whose epilogue is interpreted runs config 0 instead. */
 int b200k_gemm_num_configs(void);
 int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages);
-/* The configuration b200k_gemm_epilogue picks for a problem when tile_config is -1. */
+/* The configuration b200k_gemm_epilogue picks for a problem with a compiled
+ * epilogue when tile_config is -1 (interpreted epilogues choose among 0, 1). */
 int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K);
 
 /*

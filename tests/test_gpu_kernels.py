@@ -145,13 +145,15 @@ def test_gemm_sweep_configs(shape, act, path):
 
 @pytest.mark.parametrize("M,N,K", [(1, 8, 8), (37, 72, 24), (128, 256, 64), (130, 260, 72), (300, 100, 136),
                                    (257, 1000, 768), (64, 4096, 1024)])
-@pytest.mark.parametrize("config", [0, 1])
+@pytest.mark.parametrize("config", [0, 1, 2])
 @pytest.mark.parametrize("ab", ["bfloat16", "float16"])
 @pytest.mark.parametrize("path", ["compiled", "interpreted"])
 def test_gemm_edge_shapes(M, N, K, config, ab, path):
     """Ragged M/N/K (partial tiles, K tail inside a 64-wide block, M < 128,
-    N whose rows are not 16-byte multiples -> direct-store path), both tile
-    configs, both operand dtypes, gelu-tanh + bias + residual."""
+    N whose rows are not 16-byte multiples -> direct-store path), every tile
+    config (an interpreted epilogue forced to 192-wide tiles runs 256-wide
+    ones), both operand dtypes,
+    gelu-tanh + bias + residual."""
     dt = _tdt(ab)
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
     x = torch.randn(M, K, device=DEV, generator=g).to(dt)
@@ -167,6 +169,23 @@ def test_gemm_edge_shapes(M, N, K, config, ab, path):
     want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
                                 [b.float().cpu().numpy(), r.float().cpu().numpy()], ab, bias=b.float().cpu().numpy())
     _assert_close(out, want, *_gemm_tol(want))
+
+
+def test_gemm_192_tiles_with_interpreted_epilogue_run_config_0():
+    """Forcing the 192-wide config for an epilogue that is interpreted runs
+    the 256-wide config instead, with the same result."""
+    g = torch.Generator(device=DEV).manual_seed(5)
+    x = torch.randn(200, 64, device=DEV, generator=g).to(torch.bfloat16)
+    w = torch.randn(192, 64, device=DEV, generator=g).to(torch.bfloat16)
+    b = torch.randn(192, device=DEV, generator=g).to(torch.bfloat16)
+    code, imm, _, _ = epilogue_program("none", residual=False)
+    outs = []
+    for cfg in (2, 0):
+        out = torch.empty(200, 192, device=DEV, dtype=torch.bfloat16)
+        cabi.gemm_epilogue(x, w.t(), [b], code, imm, out, tile_config=cfg)
+        outs.append(out)
+    torch.cuda.synchronize()
+    assert torch.equal(outs[0], outs[1])
 
 
 def role_program(act: str, role: str, round_to: str | None):
@@ -188,7 +207,7 @@ def role_program(act: str, role: str, round_to: str | None):
 @pytest.mark.parametrize("act", ["none", "silu", "gelu"])
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
 @pytest.mark.parametrize("rounded", [True, False])
-@pytest.mark.parametrize("config", [0, 1])
+@pytest.mark.parametrize("config", [0, 1, 2])
 def test_gemm_row_operand_roles(role, act, dt, rounded, config):
     """A full 16-bit matrix as residual or scale, after an activation that is
     (rounded) or is not rounded to the output type first.  Rounded, the
@@ -210,7 +229,8 @@ def test_gemm_row_operand_roles(role, act, dt, rounded, config):
     for path in ("compiled", "interpreted"):
         out = torch.empty(M, N, device=DEV, dtype=t)
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
-        cabi.gemm_epilogue(x, w.t(), [b, m], code, imm, out, tile_config=config, status=status,
+        cfg = 0 if (config == 2 and path == "interpreted") else config  # 192-wide: compiled only
+        cabi.gemm_epilogue(x, w.t(), [b, m], code, imm, out, tile_config=cfg, status=status,
                            form=form if path == "compiled" else None)
         torch.cuda.synchronize()
         assert status.item() == 0

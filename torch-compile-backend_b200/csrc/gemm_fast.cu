@@ -1,5 +1,5 @@
 // Compiled-epilogue GEMM kernels for one (tile width, activation) pair.  The
-// build compiles this file once per pair, defining B200K_FAST_BN (256 or 128)
+// build compiles this file once per pair, defining B200K_FAST_BN (256, 192 or 128)
 // and B200K_FAST_ACT (a B200K_ACT_* value), so the instantiations compile in
 // parallel.  Each object defines launch_fast_<BN>_<ACT>, which covers K-major
 // B with 16-bit output and every row role, N-major B with 16-bit output and
@@ -7,17 +7,22 @@
 #include "gemm_kernel.cuh"
 
 #if !defined(B200K_FAST_BN) || !defined(B200K_FAST_ACT)
-#error "compile with -DB200K_FAST_BN=<256|128> -DB200K_FAST_ACT=<activation>"
+#error "compile with -DB200K_FAST_BN=<256|192|128> -DB200K_FAST_ACT=<activation>"
 #endif
 
 namespace b200k {
 namespace gemm {
 namespace {
 
+constexpr int config_of(int bn) {
+  for (int c = 0; c < kNumConfigs; ++c)
+    if (kConfigs[c].bn == bn) return c;
+  return -1;
+}
 constexpr int kBN = B200K_FAST_BN;
-constexpr int kStages = kBN == 256 ? kConfigs[0].stages : kConfigs[1].stages;
+static_assert(config_of(kBN) >= 0, "B200K_FAST_BN is one of the tile configs");
+constexpr int kStages = kConfigs[config_of(kBN)].stages;
 constexpr int kAct = B200K_FAST_ACT;
-static_assert((kBN == 256 && kConfigs[0].bn == 256) || (kBN == 128 && kConfigs[1].bn == 128), "tile configs");
 
 template <bool BNM>
 int launch_row16(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p,

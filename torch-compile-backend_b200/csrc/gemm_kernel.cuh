@@ -18,9 +18,10 @@
 //               tcgen05.commit -> empty[s], and hands a finished accumulator to
 //               the epilogue with tcgen05.commit -> tmem_full[acc].
 //   warp 2      owns the TMEM allocation (2*BN columns).
-//   warps 4..11 epilogue, two warps per SM sub-partition: warp w reads TMEM
-//               lane quarter (w % 4) and one half of the tile's columns with
-//               tcgen05.ld (one output row per thread), runs the epilogue
+//   warps 4..   epilogue, NG warps per SM sub-partition (NG = 2 column
+//               groups for 256- and 128-wide tiles, 3 for 192-wide ones):
+//               warp w reads TMEM lane quarter (w % 4) and one column group
+//               of the tile with tcgen05.ld (one output row per thread), runs the epilogue
 //               program in registers (bias, activation, residual, scale,
 //               casts) while the next 8 columns' operands are in flight, packs
 //               to the output dtype into a swizzled smem tile and stores it
@@ -50,9 +51,18 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of 16-bit elements
 constexpr int UMMA_K = 16;
-constexpr int kEpiWarps = 8;               // two per SM sub-partition
-constexpr int kThreads = 128 + 32 * kEpiWarps;  // warps 0-3 control, 4.. epilogue
 constexpr int kGroupM = 16;
+
+// Epilogue warp layout of a BN-wide tile: NG column groups of CW columns,
+// one warp per (TMEM lane quarter, column group); warps 0-3 are control.
+template <int BN>
+struct Epi {
+  static constexpr int NG = BN == 192 ? 3 : 2;
+  static constexpr int CW = BN / NG;  // a multiple of 64: whole 128-byte staging rows of 16-bit output
+  static constexpr int kWarps = 4 * NG;
+  static constexpr int kThreads = 128 + 32 * kWarps;
+  static_assert(CW % 64 == 0, "column groups are whole staging rows");
+};
 constexpr uint32_t kStgBytes = 32 * 128;  // one epilogue warp's 32 rows x 128 bytes
 
 struct EpiOperand {
@@ -497,14 +507,14 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 }
 
 // Warms L2 with this lane's row of the full-matrix operand (residual or
-// scale) for the tile at (m, n): the warp's BN/2 columns, which the
+// scale) for the tile at (m, n): the warp's CW columns, which the
 // sub-chunks later read straight into registers.  Issued one tile ahead, so
 // those reads wait on L2 rather than DRAM.
-template <int BN, int ROW>
+template <int CW, int ROW>
 __device__ __forceinline__ void prefetch_row16_l2(const Params& p, int m, int n) {
   if (ROW == ROW_NONE || m >= p.M || n >= p.N) return;
   const EpiOperand& e = p.ex[p.row_idx];
-  const int bytes = min(BN / 2, p.N - n) * 2;
+  const int bytes = min(CW, p.N - n) * 2;
   const char* row = reinterpret_cast<const char*>(e.ptr) + (static_cast<int64_t>(m) * e.sm + n) * 2;
   for (int off = 0; off < bytes; off += 128) prefetch_l2(row + off);
   prefetch_l2(row + bytes - 1);  // the line of the last byte when the row is not 128-byte aligned
@@ -555,7 +565,7 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
                                                int n, int s, int lane, uint8_t* sb, const FastOps& use,
                                                bool stamp_subs) {
   constexpr int kEC = 128 / OUT_BYTES;
-  constexpr int NSUB = (BN / 2) / 32;
+  constexpr int NSUB = Epi<BN>::CW / 32;
   constexpr int SUB_PER_STG = kEC / 32;
   constexpr bool kPacked = ROW == ROW_SCALE_PK || ROW == ROW_RES_PK;
   constexpr bool kMul = ROW == ROW_SCALE || ROW == ROW_SCALE_PK;
@@ -631,18 +641,19 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
 template <int BN, int OUT_BYTES, int ACT, int ROW>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
                                                    uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
-                                                   int half, int lane, const Ctl& ctl) {
-  constexpr int NSUB = (BN / 2) / 32;  // 32-column sub-chunks per warp and tile
+                                                   int cg, int lane, const Ctl& ctl) {
+  constexpr int CW = Epi<BN>::CW;
+  constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and tile
   FastOps cur{}, nxt{};
   if (static_cast<int>(blockIdx.x) < p.num_tiles) {
     int tm, tn;
     tile_coords(blockIdx.x, p, tm, tn);
-    prefetch_row16_l2<BN, ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2));
-    fast_prefetch<ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + half * (BN / 2), lane, cur);
+    prefetch_row16_l2<CW, ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + cg * CW);
+    fast_prefetch<ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + cg * CW, lane, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
-  const bool stamper = quarter == 0 && half == 0 && lane == 0;
+  const bool stamper = quarter == 0 && cg == 0 && lane == 0;
   int ti = 0;
   for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++ti) {
     int tm, tn;
@@ -653,17 +664,17 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       int tm2, tn2;
       tile_coords(t + gridDim.x, p, tm2, tn2);
       m2 = tm2 * BM + quarter * 32 + lane;
-      n2 = tn2 * BN + half * (BN / 2);
-      prefetch_row16_l2<BN, ROW>(p, m2, n2);
+      n2 = tn2 * BN + cg * CW;
+      prefetch_row16_l2<CW, ROW>(p, m2, n2);
     }
     if (!wait_bar(&tfull[acc], aph, ctl)) break;
     tc_fence_after();
     if (stamper) stamp_tile(p, ti, 4);
     const int row0 = tm * BM + quarter * 32;
     const int m = row0 + lane;
-    const int n0 = tn * BN + half * (BN / 2);
+    const int n0 = tn * BN + cg * CW;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                           static_cast<uint32_t>(acc * BN + half * (BN / 2));
+                           static_cast<uint32_t>(acc * BN + cg * CW);
 #pragma unroll 1
     for (int s = 0; s < NSUB; ++s) {
       const int n = n0 + s * 32;
@@ -690,17 +701,17 @@ template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES>
 struct Cfg {
   static constexpr uint32_t kABytes = BM * BK * 2;
   static constexpr uint32_t kBBytes = BN * BK * 2;
-  static constexpr uint32_t kTmemCols = 2 * BN;
+  static constexpr uint32_t kTmemCols = BN == 128 ? 256 : 512;  // two accumulators, power-of-two allocation
   static constexpr int kEC = 128 / OUT_BYTES;  // output columns per 128-byte staging row
-  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + kEpiWarps * kStgBytes;
+  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<BN>::kWarps * kStgBytes;
   static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
-  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM columns must be a power of two");
+  static_assert(2 * BN <= kTmemCols, "two accumulators fit the allocation");
 };
 
 template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
     gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
   using C = Cfg<BN, STAGES, B_NMAJOR, OUT_BYTES>;
@@ -729,7 +740,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], kEpiWarps);
+      mbar_init(&tempty[a], Epi<BN>::kWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -847,10 +858,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue (compiled form)
     const int ew = warp - 4;
     epilogue_fast_loop<BN, OUT_BYTES, ACT, ROW>(p, &tmO, tmem_base, tfull, tempty, sStg + ew * kStgBytes, warp & 3,
-                                           ew >> 2, lane, ctl);
+                                                ew >> 2, lane, ctl);
     } else {
     // ------------------------------------------------------------ epilogue (interpreted program)
     // Warp w reads TMEM lane quarter (w % 4) and one half of the tile's columns.
+    static_assert(Epi<BN>::NG == 2, "the interpreted epilogue runs on 256- and 128-wide tiles");
     const int ew = warp - 4;
     const int quarter = warp & 3;
     const int half = ew >> 2;
@@ -918,7 +930,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 struct TileConfig {
   int bn, stages;
 };
-constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}};
+// Config 2 (192-wide tiles, twelve epilogue warps) exists for compiled epilogues only.
+constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}, {192, 4}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
 template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW>
@@ -932,7 +945,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& 
       return B200K_ERR_LAUNCH;
     attr_set = true;
   }
-  kern<<<grid, kThreads, C::kSmem, st>>>(ta, tb, to, p);
+  kern<<<grid, Epi<BN>::kThreads, C::kSmem, st>>>(ta, tb, to, p);
   return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
 }
 
@@ -957,6 +970,11 @@ B200K_DECLARE_FAST(128, 1)
 B200K_DECLARE_FAST(128, 2)
 B200K_DECLARE_FAST(128, 3)
 B200K_DECLARE_FAST(128, 4)
+B200K_DECLARE_FAST(192, 0)
+B200K_DECLARE_FAST(192, 1)
+B200K_DECLARE_FAST(192, 2)
+B200K_DECLARE_FAST(192, 3)
+B200K_DECLARE_FAST(192, 4)
 #undef B200K_DECLARE_FAST
 
 }  // namespace gemm

@@ -72,22 +72,34 @@ int launch_fast(int bn, int act, bool bnm, int ob, int row, const CUtensorMap& t
   B200K_FAST_CASE(128, 2)
   B200K_FAST_CASE(128, 3)
   B200K_FAST_CASE(128, 4)
+  B200K_FAST_CASE(192, 0)
+  B200K_FAST_CASE(192, 1)
+  B200K_FAST_CASE(192, 2)
+  B200K_FAST_CASE(192, 3)
+  B200K_FAST_CASE(192, 4)
 #undef B200K_FAST_CASE
   return B200K_ERR_UNSUPPORTED;
 }
 
-int pick(int64_t M, int64_t N, int sms) {
+int pick(int64_t M, int64_t N, int sms, bool compiled) {
   // Per-SM time of a config ~ (tiles per SM, rounded up) x (tile width) x
   // (cost per column).  Measured on B200 (bias + residual epilogue, 4096^3):
   // 128x256 tiles, 4 waves: 0.134 ms; 128x128 tiles, 7 waves: 0.173 ms, i.e.
   // the narrow tile does ~1.5x less work per unit time (it re-reads A twice as
-  // often, runs the MMA at N=128 and pays the epilogue per tile twice).
+  // often, runs the MMA at N=128 and pays the epilogue per tile twice).  The
+  // 192-wide tile (compiled epilogues only) spreads its epilogue over twelve
+  // warps and loses little per column; it wins where 256-wide tiles leave a
+  // mostly idle last wave (N = 768: 297 tiles on 148 SMs = 3 waves, against
+  // 396 tiles of 3/4 the work = 3 shorter waves).
   int best = 0;
   double best_cost = 1e300;
   for (int c = 0; c < kNumConfigs; ++c) {
-    const int64_t tiles = ((M + BM - 1) / BM) * ((N + kConfigs[c].bn - 1) / kConfigs[c].bn);
+    const int bn = kConfigs[c].bn;
+    if (bn == 192 && !compiled) continue;
+    const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
     const int64_t per_sm = (tiles + sms - 1) / sms;
-    const double cost = static_cast<double>(per_sm) * kConfigs[c].bn * (kConfigs[c].bn == 256 ? 1.0 : 1.5);
+    const double per_col = bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5);
+    const double cost = static_cast<double>(per_sm) * bn * per_col;
     if (cost < best_cost) {
       best_cost = cost;
       best = c;
@@ -129,7 +141,7 @@ extern "C" int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K) {
   (void)K;
   int sms = device_sm_count();
   if (sms <= 0) sms = 148;
-  return pick(M, N, sms);
+  return pick(M, N, sms, true);
 }
 
 extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
@@ -170,13 +182,38 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     if (!valid_dtype(a->extras[i].dtype)) return B200K_ERR_UNSUPPORTED;
   }
 
+  const int ob = a->out_dtype == B200K_F32 ? 4 : 2;
+  auto mode_of = [&](int idx, bool allow_row) -> int32_t {
+    if (idx < 0) return XM_NONE;
+    const B200kEpiOperand& e = a->extras[idx];
+    const bool f_or_16 = e.dtype == B200K_F32 || e.dtype == B200K_BF16 || e.dtype == B200K_F16;
+    if (e.stride_m == 0) return f_or_16 ? XM_BCAST : XM_GENERIC;
+    if (allow_row && e.stride_n == 1 && (e.dtype == B200K_BF16 || e.dtype == B200K_F16) && aligned16(e.ptr) &&
+        e.stride_m % 8 == 0)
+      return XM_ROW16;
+    return XM_GENERIC;
+  };
+  // Compiled path: canonical form, output storable by TMA, a row-broadcast
+  // bias (or none), at most one of scale and residual as a full 16-bit
+  // matrix of the output's type, and an activation with compiled kernels.
+  const bool tma_out = aligned16(a->out) && (a->out_stride_m * ob) % 16 == 0;
+  const int role_idx = a->form.residual >= 0 ? a->form.residual : a->form.scale;
+  const bool both = a->form.residual >= 0 && a->form.scale >= 0;
+  bool act_ok = false;
+  for (int fa : kFastActs) act_ok = act_ok || fa == a->form.act;
+  const bool row_ok = role_idx < 0 || (ob == 2 && mode_of(role_idx, true) == XM_ROW16 &&
+                                       a->extras[role_idx].dtype == a->out_dtype);
+  const int bias_mode = mode_of(a->form.bias, false);
+  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
+                    (bias_mode == XM_NONE || bias_mode == XM_BCAST);
+
   const int sms = device_sm_count();
   if (sms <= 0) return B200K_ERR_DEVICE;
   int cfg = a->tile_config;
-  if (cfg < 0) cfg = pick(a->M, a->N, sms);
+  if (cfg < 0) cfg = pick(a->M, a->N, sms, fast);
   if (cfg >= kNumConfigs) return B200K_ERR_ARG;
+  if (kConfigs[cfg].bn == 192 && !fast) cfg = 0;  // 192-wide tiles run compiled epilogues only
   const int bn = kConfigs[cfg].bn;
-  const int ob = a->out_dtype == B200K_F32 ? 4 : 2;
 
   Params p;
   std::memset(&p, 0, sizeof(p));
@@ -217,17 +254,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.f_round = a->form.round;
   p.f_scale = a->form.scale;
   p.f_res = a->form.residual;
-  auto mode_of = [&](int idx, bool allow_row) -> int32_t {
-    if (idx < 0) return XM_NONE;
-    const B200kEpiOperand& e = a->extras[idx];
-    const bool f_or_16 = e.dtype == B200K_F32 || e.dtype == B200K_BF16 || e.dtype == B200K_F16;
-    if (e.stride_m == 0) return f_or_16 ? XM_BCAST : XM_GENERIC;
-    if (allow_row && e.stride_n == 1 && (e.dtype == B200K_BF16 || e.dtype == B200K_F16) && aligned16(e.ptr) &&
-        e.stride_m % 8 == 0)
-      return XM_ROW16;
-    return XM_GENERIC;
-  };
-  p.xm_bias = mode_of(a->form.bias, false);
+  p.xm_bias = bias_mode;
   p.xm_scale = mode_of(a->form.scale, true);
   p.xm_res = mode_of(a->form.residual, true);
   p.trace = nullptr;
@@ -240,7 +267,6 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   } else {
     if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, bn)) return B200K_ERR_LAUNCH;
   }
-  const bool tma_out = aligned16(a->out) && (a->out_stride_m * ob) % 16 == 0;
   p.direct_store = tma_out ? 0 : 1;
   if (tma_out) {
     if (!make_map(&to, a->out_dtype, a->out, a->N, a->M, a->out_stride_m * ob, 128 / ob, 32)) return B200K_ERR_LAUNCH;
@@ -249,17 +275,6 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (a->trace && a->trace_words >= static_cast<int64_t>(grid) * B200K_GEMM_TRACE_WORDS)
     p.trace = reinterpret_cast<unsigned long long*>(a->trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
-  // Compiled path: canonical form, output storable by TMA, a row-broadcast
-  // bias (or none), at most one of scale and residual as a full 16-bit
-  // matrix of the output's type, and an activation with compiled kernels.
-  const int role_idx = a->form.residual >= 0 ? a->form.residual : a->form.scale;
-  const bool both = a->form.residual >= 0 && a->form.scale >= 0;
-  bool act_ok = false;
-  for (int fa : kFastActs) act_ok = act_ok || fa == a->form.act;
-  const bool row_ok = role_idx < 0 || (ob == 2 && mode_of(role_idx, true) == XM_ROW16 &&
-                                       a->extras[role_idx].dtype == a->out_dtype);
-  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
-                    (p.xm_bias == XM_NONE || p.xm_bias == XM_BCAST);
   if (fast) {
     int row = ROW_NONE;
     if (role_idx >= 0) {
