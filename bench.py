@@ -447,10 +447,14 @@ def _backend(name: str):
 
 
 def _time_device(fn, steps: int, warmup: int, flush=None) -> list[float]:
+    """Device time of each of `steps` calls (CUDA events on the current
+    stream around the call, an L2 flush between calls).  The steps are queued
+    back to back and synchronised once at the end, so the host's per-call
+    cost overlaps the device's work, as in a running model."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
-    times = []
+    ev = []
     for _ in range(steps):
         if flush is not None:
             flush.zero_()
@@ -458,9 +462,9 @@ def _time_device(fn, steps: int, warmup: int, flush=None) -> list[float]:
         e0.record()
         fn()
         e1.record()
-        torch.cuda.synchronize()
-        times.append(e0.elapsed_time(e1))
-    return times
+        ev.append((e0, e1))
+    torch.cuda.synchronize()
+    return [e0.elapsed_time(e1) for e0, e1 in ev]
 
 
 def run_model(args, dist: Dist) -> dict:

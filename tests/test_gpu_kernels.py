@@ -344,22 +344,27 @@ def test_pointwise_empty_is_noop():
 
 
 # ------------------------------------------------------------- row kernels
-@pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768)])
-def test_rms_norm_swiglu(rows, cols):
+@pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768), (9, 2048)])
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("flags", [7, 1])
+def test_rms_norm_swiglu(rows, cols, dtype, flags):
+    """16-bit rows whose half is a multiple of 8 run the specialised kernel
+    (flags 7: every rounding of the 16-bit graph); the others, and flag sets
+    it does not implement, the generic one."""
+    dt = _tdt(dtype)
     g = torch.Generator(device=DEV).manual_seed(0)
-    x = torch.randn(rows, cols, device=DEV, generator=g).to(torch.bfloat16)
-    w = (1 + 0.02 * torch.randn(cols, device=DEV, generator=g)).to(torch.bfloat16)
-    out = torch.empty(rows, cols // 2, device=DEV, dtype=torch.bfloat16)
-    cabi.rownorm(x, cabi.ROW_RMSNORM_SWIGLU, w, None, 1e-6, 7, out)
+    x = torch.randn(rows, cols, device=DEV, generator=g).to(dt)
+    w = (1 + 0.02 * torch.randn(cols, device=DEV, generator=g)).to(dt)
+    out = torch.empty(rows, cols // 2, device=DEV, dtype=dt)
+    rstd = torch.empty(rows, device=DEV)
+    cabi.rownorm(x, cabi.ROW_RMSNORM_SWIGLU, w, None, 1e-6, flags, out, rstd_out=rstd)
     torch.cuda.synchronize()
-    sel = slice(0, min(rows, 256))
-    want = oracle.rms_norm_swiglu(x[sel].float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, 7, "bfloat16",
-                                  "bfloat16")
-    _assert_close(out[sel], want, 1e-2, 1e-2)
-    if rows > 256:  # the last rows too
-        want = oracle.rms_norm_swiglu(x[-64:].float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, 7, "bfloat16",
-                                      "bfloat16")
-        _assert_close(out[-64:], want, 1e-2, 1e-2)
+    for sel in (slice(0, min(rows, 256)), slice(max(rows - 64, 0), rows)):
+        xs = x[sel].float().cpu().numpy()
+        want = oracle.rms_norm_swiglu(xs, w.float().cpu().numpy(), 1e-6, flags, dtype, dtype)
+        _assert_close(out[sel], want, 1e-2, 1e-2)
+        want_rstd = 1.0 / np.sqrt((xs.astype(np.float64) ** 2).mean(-1) + 1e-6)
+        _assert_close(rstd[sel], want_rstd, 1e-5, 0)
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
@@ -378,11 +383,13 @@ def test_rms_norm(dtype, cols):
     _assert_close(out, want, *tol)
 
 
-@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50)])
-def test_layer_norm(rows, cols):
-    x = torch.randn(rows, cols, device=DEV).to(torch.bfloat16)
-    w = torch.randn(cols, device=DEV).to(torch.bfloat16)
-    b = torch.randn(cols, device=DEV).to(torch.bfloat16)
+@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50), (5, 16384)])
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_layer_norm(rows, cols, dtype):
+    dt = _tdt(dtype)
+    x = torch.randn(rows, cols, device=DEV).to(dt)
+    w = torch.randn(cols, device=DEV).to(dt)
+    b = torch.randn(cols, device=DEV).to(dt)
     out = torch.empty_like(x)
     mean = torch.empty(rows, device=DEV)
     rstd = torch.empty(rows, device=DEV)
@@ -390,23 +397,25 @@ def test_layer_norm(rows, cols):
     torch.cuda.synchronize()
     sel = slice(0, 500)
     o, m, r = oracle.layer_norm(x[sel].float().cpu().numpy(), w.float().cpu().numpy(), b.float().cpu().numpy(), 1e-6,
-                                "bfloat16")
+                                dtype)
     _assert_close(out[sel], o, 1e-2, 2e-2)
     _assert_close(mean[sel], m[:, 0], 1e-5, 1e-5)
     _assert_close(rstd[sel], r[:, 0], 1e-4, 1e-5)
 
 
-@pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768)])
+@pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768), (6, 8192), (5, 2048)])
 @pytest.mark.parametrize("log", [False, True])
-def test_softmax(rows, cols, log):
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+def test_softmax(rows, cols, log, dtype):
     g = torch.Generator(device=DEV).manual_seed(0)
-    x = (2 * torch.randn(rows, cols, device=DEV, generator=g)).to(torch.bfloat16)
+    x = (2 * torch.randn(rows, cols, device=DEV, generator=g)).to(_tdt(dtype))
+    x[0, : min(cols, 5)] = -float("inf")  # masked entries
     out = torch.empty_like(x)
     cabi.softmax(x, out, log=log)
     torch.cuda.synchronize()
     sel = slice(0, 128)
     fn = oracle.log_softmax if log else oracle.softmax
-    want = fn(x[sel].float().cpu().numpy(), "bfloat16")
+    want = fn(x[sel].float().cpu().numpy(), dtype)
     _assert_close(out[sel], want, 1e-2, 1e-2 if log else 1e-4)
     if not log:  # every row sums to one
         s = out.float().sum(-1)

@@ -17,35 +17,12 @@
 
 #include "common.cuh"
 #include "host_common.h"
+#include "rowreduce.cuh"
 
 namespace b200k {
 
 constexpr int kVPT = 4;  // vectors per thread
 
-struct RowParams {
-  int64_t rows, cols;
-  const void* x;
-  int64_t x_stride;
-  const void* w;
-  const void* b;
-  void* out;
-  int64_t out_stride;
-  float* mean_out;
-  float* rstd_out;
-  float eps;
-  int32_t x_dt, w_dt, b_dt, out_dt, flags, log_softmax;
-};
-
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  return v;
-}
-__device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
-}
 
 // Sum (IS_MAX=false) or max over the TPR threads of a row.  Every thread of the
 // CTA must call it (it may synchronise the CTA).
@@ -443,6 +420,8 @@ extern "C" int b200k_rownorm(const B200kRowNormArgs* a, void* stream_) {
   const int tpr = pick_tpr(vec ? span / 8 : span);
   if (tpr == 0) return B200K_ERR_SHAPE;
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int rc16 = launch_row16(swiglu ? R16_SWIGLU : (layer ? R16_LAYERNORM : R16_RMSNORM), p, st);
+  if (rc16 >= 0) return rc16;
   const bool x16 = a->x_dtype == B200K_BF16 || a->x_dtype == B200K_F16;
   if (swiglu) return dispatch_tpr<SelSwiglu>(tpr, vec, x16, p, st);
   if (layer) return dispatch_tpr<SelLayer>(tpr, vec, x16, p, st);
@@ -470,6 +449,9 @@ extern "C" int b200k_softmax(const B200kSoftmaxArgs* a, void* stream_) {
   const bool vec = row_vec_ok(a->x, a->x_row_stride, a->cols) && row_vec_ok(a->out, a->out_row_stride, a->cols);
   const int tpr = pick_tpr(vec ? a->cols / 8 : a->cols);
   if (tpr == 0) return B200K_ERR_SHAPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  const int rc16 = launch_row16(a->log_softmax ? R16_LOG_SOFTMAX : R16_SOFTMAX, p, st);
+  if (rc16 >= 0) return rc16;
   const bool x16 = a->x_dtype == B200K_BF16 || a->x_dtype == B200K_F16;
-  return dispatch_tpr<SelSoftmax>(tpr, vec, x16, p, static_cast<cudaStream_t>(stream_));
+  return dispatch_tpr<SelSoftmax>(tpr, vec, x16, p, st);
 }
