@@ -312,6 +312,34 @@ typedef struct {
 
 int b200k_softmax(const B200kSoftmaxArgs* args, void* stream);
 
+/* Rotary position embedding, rotate-half form (an extension: the reference
+ * has no counterpart; its pointwise pass leaves the aten.cat of rotate_half
+ * in ATen and fuses only x*cos + r*sin):
+ *   out = x * cos + rotate_half(x) * sin,
+ *   rotate_half(x)[..., j] = -x[..., j + D/2] for j < D/2, x[..., j - D/2] after,
+ * over a rank-4 index space [B, H, S, D] (lower ranks padded with size-1
+ * dims).  x, cos, sin and out are all bf16 or all f16, with any element
+ * strides (0 broadcasts cos / sin).  Each product
+ * and the sum round to that type, as the decomposed graph does, so the
+ * result equals eager PyTorch bit for bit.  D even.  With D a multiple of 16,
+ * unit stride in D and 16-byte aligned pointers and outer strides, each
+ * thread moves 8 elements; any other layout runs an element-wise kernel. */
+typedef struct {
+  int64_t sizes[4];
+  const void* x;
+  int64_t x_strides[4];
+  const void* cos;
+  int64_t cos_strides[4];
+  const void* sin;
+  int64_t sin_strides[4];
+  void* out;
+  int64_t out_strides[4];
+  int32_t dtype;
+  int32_t pad;
+} B200kRopeArgs;
+
+int b200k_rope(const B200kRopeArgs* args, void* stream);
+
 const char* b200k_status_string(int code);
 /* Library version, for the loader's sanity check. */
 int b200k_version(void);

@@ -66,6 +66,13 @@ def test_host_side_errors_need_no_gpu():
     assert lib.b200k_rownorm(ctypes.byref(r), None) == 1  # null x / out
     r.rows = 0
     assert lib.b200k_rownorm(ctypes.byref(r), None) == 0  # empty: nothing to do
+    q = cabi.RopeArgs()
+    q.sizes[:] = [1, 2, 3, 64]
+    assert lib.b200k_rope(ctypes.byref(q), None) == 1  # null pointers
+    q.sizes[3] = 0
+    assert lib.b200k_rope(ctypes.byref(q), None) == 0  # empty: nothing to do
+    q.sizes[3] = -1
+    assert lib.b200k_rope(ctypes.byref(q), None) == 3  # B200K_ERR_SHAPE
 
 
 STRUCTS = {
@@ -81,6 +88,8 @@ STRUCTS = {
     "B200kRowNormArgs": (cabi.RowNormArgs, ["rows", "x", "kind", "weight", "flags", "bias", "eps", "out",
                                             "out_dtype", "mean_out", "rstd_out"]),
     "B200kSoftmaxArgs": (cabi.SoftmaxArgs, ["rows", "x", "log_softmax", "out", "out_dtype"]),
+    "B200kRopeArgs": (cabi.RopeArgs, ["sizes", "x", "x_strides", "cos", "cos_strides", "sin", "sin_strides", "out",
+                                      "out_strides", "dtype"]),
 }
 
 

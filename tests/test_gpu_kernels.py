@@ -433,3 +433,50 @@ def test_gemm_rejects_form_that_contradicts_program():
     with pytest.raises(cabi.CError) as e:
         cabi.gemm_epilogue(x, w.t(), [b], code, imm, out, form=bad)
     assert e.value.code == 7
+
+
+# ------------------------------------------------------------- rotary embedding
+def _rope_eager(x, c, s):
+    x1, x2 = x.chunk(2, dim=-1)
+    return x * c + torch.cat((-x2, x1), dim=-1) * s
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("case", ["llama_q", "llama_k", "hf_bcast", "d128", "unaligned", "odd_half"])
+def test_rope_matches_eager_bit_for_bit(dtype, case):
+    """b200k_rope against eager PyTorch's decomposed rotate-half graph on the
+    same inputs: products and sum round to the 16-bit type in both, so the
+    results are equal bit for bit -- on the 8-wide path (transposed q / k
+    views with a [S, D] table, [B, 1, S, D] tables, D = 128) and on the
+    element-wise path (a view one element off 16-byte alignment, D / 2 not a
+    multiple of 8)."""
+    dt = _tdt(dtype)
+    g = torch.Generator(device=DEV).manual_seed(7)
+    B, S = 2, 256
+    if case in ("llama_q", "llama_k"):
+        H = 32 if case == "llama_q" else 8
+        x = torch.randn(B, S, H, 64, device=DEV, generator=g).to(dt).transpose(1, 2)
+        c, s = (torch.randn(S, 64, device=DEV, generator=g).to(dt) for _ in range(2))
+    elif case == "hf_bcast":
+        x = torch.randn(B, 4, S, 64, device=DEV, generator=g).to(dt)
+        c, s = (torch.randn(B, 1, S, 64, device=DEV, generator=g).to(dt) for _ in range(2))
+    elif case == "d128":
+        x = torch.randn(B, 4, S, 128, device=DEV, generator=g).to(dt)
+        c, s = (torch.randn(S, 128, device=DEV, generator=g).to(dt) for _ in range(2))
+    elif case == "unaligned":
+        base = torch.randn(B * 4 * S * 64 + 1, device=DEV, generator=g).to(dt)
+        x = base[1:].view(B, 4, S, 64)
+        c, s = (torch.randn(S, 64, device=DEV, generator=g).to(dt) for _ in range(2))
+    else:
+        x = torch.randn(B, 4, S, 20, device=DEV, generator=g).to(dt)
+        c, s = (torch.randn(S, 20, device=DEV, generator=g).to(dt) for _ in range(2))
+    want = _rope_eager(x, c, s)
+    out = torch.empty_strided(want.shape, want.stride(), device=DEV, dtype=dt)
+    cabi.rope(x, c, s, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out, want)
+    ref = oracle.rope(x.float().cpu().numpy(), c.float().cpu().numpy(), s.float().cpu().numpy(), dtype)
+    np.testing.assert_array_equal(out.float().cpu().numpy(), ref)
+    # and through the torch op with the decomposed graph's layout
+    got = torch.ops.b200.rope(x, c, s, list(want.stride()))
+    assert got.stride() == want.stride() and torch.equal(got, want)

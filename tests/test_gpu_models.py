@@ -82,7 +82,11 @@ def test_llama_small_bf16():
         got = torch.compile(model, backend=be)(ids)
     t = [str(s) for s in b200_targets(graphs)]
     assert "b200.rms_norm.default" in t
-    assert "b200.gemm_epilogue.default" in t
+    assert t.count("b200.rope.default") == 2 * 2  # q and k rotations per layer
+    # per layer: o + residual, gate (silu * up), down + residual, all on the compiled path
+    epi = [n for g in graphs for n in g.graph.nodes if n.op == "call_function"
+           and n.target == torch.ops.b200.gemm_epilogue.default]
+    assert len(epi) == 3 * 2 and all(list(n.args[7]) for n in epi)
     assert _rel(got, want) < 2e-2
 
 

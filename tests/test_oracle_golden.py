@@ -93,3 +93,17 @@ def test_rowreduce_oracles_match_torch_cpu():
                                atol=1e-7)
     np.testing.assert_allclose(oracle.log_softmax(xs.numpy(), "float32"), torch.log_softmax(xs, -1).numpy(),
                                rtol=1e-5, atol=1e-5)
+
+
+def test_rope_oracle_matches_torch_cpu_bit_for_bit():
+    import torch
+
+    g = torch.Generator().manual_seed(0)
+    for dt, name in ((torch.bfloat16, "bfloat16"), (torch.float16, "float16")):
+        x = torch.randn(2, 4, 16, 64, generator=g).to(dt)
+        c = torch.randn(16, 64, generator=g).to(dt)
+        s = torch.randn(16, 64, generator=g).to(dt)
+        x1, x2 = x.chunk(2, dim=-1)
+        ref = x * c + torch.cat((-x2, x1), dim=-1) * s
+        got = oracle.rope(x.float().numpy(), c.float().numpy(), s.float().numpy(), name)
+        np.testing.assert_array_equal(got, ref.float().numpy())

@@ -274,6 +274,23 @@ def test_canonical_form_variants():
     assert list(n.args[7]) == []  # interpreted
 
 
+def test_residual_without_bias_takes_the_residual_role():
+    """x + o(a) with a bias-free Linear: the full [M, N] operand is the
+    residual (streamed by the compiled path), never the bias, which only a
+    row vector can be."""
+    class Res(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.o = nn.Linear(64, 64, bias=False)
+
+        def forward(self, x, a):
+            return x + self.o(a)
+
+    x = torch.randn(2, 8, 64).to(torch.bfloat16)
+    forms = [list(n.args[7]) for n in _epi_nodes(Res().to(torch.bfloat16), (x, x.clone()))]
+    assert forms == [[1, -1, 0, -1, -1, 0]]
+
+
 def test_llama_gate_up_epilogue_is_canonical():
     """silu(gate(h)) * up(h): the gate GEMM's epilogue multiplies by the up GEMM output."""
     class SwiGLU(nn.Module):
@@ -301,3 +318,71 @@ def test_pointwise_keeps_permuted_layout():
     (gm,) = fused_graphs(Rope(), (q, c, c))
     n = next(n for n in gm.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.pointwise.default)
     assert list(n.args[5]) == list(n.meta["val"].stride()) and not n.meta["val"].is_contiguous()
+
+
+class _RopeLlama(nn.Module):
+    """Llama's rotate_half (chunk -> split) on a transposed q."""
+
+    def forward(self, q, c, s):
+        q = q.transpose(1, 2)
+        x1, x2 = q.chunk(2, dim=-1)
+        return q * c + torch.cat((-x2, x1), dim=-1) * s
+
+
+class _RopeHF(nn.Module):
+    """The slice form of rotate_half, cos / sin broadcast from [B, 1, S, D]."""
+
+    def forward(self, q, c, s):
+        x1 = q[..., : q.shape[-1] // 2]
+        x2 = q[..., q.shape[-1] // 2:]
+        return (q * c) + (torch.cat((-x2, x1), dim=-1) * s)
+
+
+def _rope_nodes(gm):
+    return [n for n in gm.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.rope.default]
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+def test_rope_pass_replaces_rotate_half_group(dt):
+    q = torch.randn(2, 16, 4, 64).to(dt)
+    c = torch.randn(16, 64).to(dt)
+    (gm,) = fused_graphs(_RopeLlama(), (q, c, c.clone()))
+    (n,) = _rope_nodes(gm)
+    ops = {str(m.target) for m in gm.graph.nodes if m.op == "call_function"}
+    assert not any(k in o for o in ops for k in ("cat", "neg", "split", "mul", "add"))
+    eager = _RopeLlama()(q, c, c)
+    assert list(n.args[3]) == list(eager.stride())  # the decomposed graph's layout
+    q2 = torch.randn(2, 4, 16, 64).to(dt)
+    c2 = torch.randn(2, 1, 16, 64).to(dt)
+    (gm,) = fused_graphs(_RopeHF(), (q2, c2, c2.clone()))
+    assert len(_rope_nodes(gm)) == 1
+
+
+def test_rope_pass_leaves_other_chains():
+    q = torch.randn(2, 16, 4, 64)
+    c = torch.randn(16, 64)
+    (gm,) = fused_graphs(_RopeLlama(), (q, c, c.clone()))  # fp32: no fused kernel for it
+    assert not _rope_nodes(gm)
+
+    class Swapped(nn.Module):  # cat(x1, -x2) is not rotate_half
+        def forward(self, q, c, s):
+            q = q.transpose(1, 2)
+            x1, x2 = q.chunk(2, dim=-1)
+            return q * c + torch.cat((x1, -x2), dim=-1) * s
+
+    qb, cb = q.to(torch.bfloat16), c.to(torch.bfloat16)
+    (gm,) = fused_graphs(Swapped(), (qb, cb, cb.clone()))
+    assert not _rope_nodes(gm)
+    (gm,) = fused_graphs(_RopeLlama(), (qb, cb, cb.clone()), extensions=False)
+    assert not _rope_nodes(gm)
+
+
+def test_llama_layer_fuses_both_rotations():
+    import bench_models as bm
+
+    layer = bm.LlamaLayer(128, 4, 2, 256, 1e-5).to(torch.bfloat16)
+    m = bm.Llama(vocab=32, dim=128, layers=1, heads=4, kv_heads=2, ffn=256, max_seq=16)
+    x = torch.randn(1, 16, 128).to(torch.bfloat16)
+    cos, sin = m.cos[:16].to(torch.bfloat16), m.sin[:16].to(torch.bfloat16)
+    graphs = fused_graphs(layer, (x, cos, sin))
+    assert sum(len(_rope_nodes(g)) for g in graphs) == 2

@@ -21,6 +21,7 @@ from compiler import runtime
 from compiler.optimization import config
 from compiler.optimization.fusion_epilogue import fuse_epilogue
 from compiler.optimization.fusion_pointwise import fuse_pointwise
+from compiler.optimization.fusion_rope import fuse_rope
 from compiler.optimization.fusion_rowreduce import fuse_rowreduce
 
 runtime.load()
@@ -39,6 +40,9 @@ def compiler(gm: fx.GraphModule, example_inputs):
     if config.EXTENSIONS and config.ENABLE_ROWREDUCE:
         gm = fuse_rowreduce(gm)  # whole row groups (extension; runs first so the
         #                          pointwise passes do not split them)
+    if config.EXTENSIONS and config.ENABLE_ROPE:
+        gm = fuse_rope(gm)  # x*cos + rotate_half(x)*sin (extension; before the
+        #                     pointwise pass would take its multiply-add)
     if config.ENABLE_EPILOGUE:
         gm = fuse_epilogue(gm)  # pointwise groups that consume a matmul
     if config.ENABLE_POINTWISE:

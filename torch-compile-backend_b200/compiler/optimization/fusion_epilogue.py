@@ -159,9 +159,21 @@ def build_epilogue_op(group, matmul, inputs, anchor=None):
     return prog, [int(s) for s in out_meta.shape], out_meta.dtype
 
 
-def epilogue_form(prog, n_operands: int) -> list[int]:
-    """The kernel's compiled-path descriptor for this program ([] = interpret)."""
-    form = canonical_form(prog, n_operands) if config.FAST_EPILOGUE else None
+def _row_vector(n) -> bool:
+    """An epilogue operand that broadcasts along the rows of the [M, N] output."""
+    v = _tensor_meta(n) if isinstance(n, fx.Node) else None
+    if v is None:
+        return False
+    shape = list(v.shape)
+    return len(shape) <= 1 or all(s == 1 for s in shape[:-1])
+
+
+def epilogue_form(prog, n_operands: int, operands=None) -> list[int]:
+    """The kernel's compiled-path descriptor for this program ([] = interpret).
+    ``operands`` (the extras, in slot order 1..) lets only row vectors take the
+    bias role."""
+    rv = None if operands is None else [False] + [_row_vector(n) for n in operands]
+    form = canonical_form(prog, n_operands, rv) if config.FAST_EPILOGUE else None
     return form or []
 
 
@@ -197,7 +209,8 @@ def fuse_epilogue(gm: fx.GraphModule) -> fx.GraphModule:
         with gm.graph.inserting_before(root):
             new_node = gm.graph.call_function(
                 torch.ops.b200.gemm_epilogue.default,
-                (mat1, mat2, list(inputs), prog.code, prog.imm, shape, dtype, epilogue_form(prog, 1 + len(inputs))),
+                (mat1, mat2, list(inputs), prog.code, prog.imm, shape, dtype,
+                 epilogue_form(prog, 1 + len(inputs), list(inputs))),
             )
         new_node.meta = dict(root.meta)
         new_node.meta["b200_kernel"] = new_kernel_name("gemm_epilogue")

@@ -371,9 +371,15 @@ def symbolic(code: list[int], imm: list[float], n_operands: int):
     return acc
 
 
-def canonical_form(prog: Program, n_operands: int) -> list[int] | None:
+def canonical_form(prog: Program, n_operands: int, row_vector: list[bool] | None = None) -> list[int] | None:
     """[1, bias, act, round, scale, residual] (extras indices, -1 = absent) when
-    the GEMM-epilogue program (slot 0 = accumulator) has the canonical form."""
+    the GEMM-epilogue program (slot 0 = accumulator) has the canonical form.
+
+    ``row_vector[i]`` (operand i, slot 0 being the accumulator) says whether
+    operand i broadcasts along rows (a [N] or [1, N] vector).  Only such an
+    operand can be the bias: without an activation ``acc + x`` reads either
+    way, and a full [M, N] matrix belongs in the residual role, whose kernel
+    path streams it.  None = no restriction."""
     tree = symbolic(prog.code, prog.imm, n_operands)
 
     def peel(t, op):
@@ -392,7 +398,7 @@ def canonical_form(prog: Program, n_operands: int) -> list[int] | None:
                 rounds.append((t2[1], _DT_F16))
             for t3, rnd in rounds:
                 for act, tmpl in _ACT_TEMPLATES.items():
-                    for bias in [-1] + list(range(1, n_operands)):
+                    for bias in [-1] + [i for i in range(1, n_operands) if row_vector is None or row_vector[i]]:
                         base = ("in", 0) if bias < 0 else _mk("add", ("in", 0), ("in", bias))
                         if tmpl(base) == t3:
                             return [1, bias - 1 if bias > 0 else -1, ACT_CODES[act], rnd,

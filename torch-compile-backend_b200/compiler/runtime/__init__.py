@@ -75,6 +75,12 @@ def _register_fakes() -> None:
     def _(x, dim, half_to_float):
         return x.new_empty(x.shape, dtype=torch.float32 if half_to_float else x.dtype)
 
+    @torch.library.register_fake(lib + "rope")
+    def _(x, cos, sin, out_stride=()):
+        if out_stride:
+            return x.new_empty_strided(x.shape, out_stride)
+        return x.new_empty(x.shape)
+
 
 def gemm_status(device: int = 0, reset: bool = True) -> int:
     """The GEMM kernels' device status word (0 = ok, 6 = a wait timed out);

@@ -28,7 +28,7 @@ ROW_RMSNORM, ROW_LAYERNORM, ROW_RMSNORM_SWIGLU = 0, 1, 2
 EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
-    "b200k_gemm_epilogue_noalloc",
+    "b200k_gemm_epilogue_noalloc", "b200k_rope",
 ]
 
 
@@ -91,6 +91,13 @@ class SoftmaxArgs(ctypes.Structure):
                 ("pad", ctypes.c_int32)]
 
 
+class RopeArgs(ctypes.Structure):
+    _fields_ = [("sizes", ctypes.c_int64 * 4), ("x", ctypes.c_void_p), ("x_strides", ctypes.c_int64 * 4),
+                ("cos", ctypes.c_void_p), ("cos_strides", ctypes.c_int64 * 4), ("sin", ctypes.c_void_p),
+                ("sin_strides", ctypes.c_int64 * 4), ("out", ctypes.c_void_p), ("out_strides", ctypes.c_int64 * 4),
+                ("dtype", ctypes.c_int32), ("pad", ctypes.c_int32)]
+
+
 _lib = None
 
 
@@ -106,6 +113,7 @@ def library() -> ctypes.CDLL:
             ("b200k_gemm_epilogue_noalloc", [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
             ("b200k_rownorm", [ctypes.POINTER(RowNormArgs), ctypes.c_void_p]),
             ("b200k_softmax", [ctypes.POINTER(SoftmaxArgs), ctypes.c_void_p]),
+            ("b200k_rope", [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
             ("b200k_gemm_pick_config", [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
             ("b200k_gemm_config_info", [ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
             ("b200k_gemm_num_configs", []),
@@ -232,3 +240,20 @@ def softmax(x: torch.Tensor, out: torch.Tensor, log: bool = False) -> None:
     a.log_softmax = 1 if log else 0
     a.out, a.out_row_stride, a.out_dtype = out.data_ptr(), (out.stride(-2) if out.dim() > 1 else a.cols), DTYPE[out.dtype]
     _check("b200k_softmax", library().b200k_softmax(ctypes.byref(a), _stream()))
+
+
+def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor) -> None:
+    """out = x * cos + rotate_half(x) * sin (rank <= 4; cos / sin broadcast to x)."""
+    c, sn = cos.expand(x.shape), sin.expand(x.shape)
+    a = RopeArgs()
+    pad = 4 - x.dim()
+    for d in range(4):
+        real = d >= pad
+        a.sizes[d] = x.shape[d - pad] if real else 1
+        a.x_strides[d] = x.stride(d - pad) if real else 0
+        a.cos_strides[d] = c.stride(d - pad) if real else 0
+        a.sin_strides[d] = sn.stride(d - pad) if real else 0
+        a.out_strides[d] = out.stride(d - pad) if real else 0
+    a.x, a.cos, a.sin, a.out = x.data_ptr(), c.data_ptr(), sn.data_ptr(), out.data_ptr()
+    a.dtype = DTYPE[x.dtype]
+    _check("b200k_rope", library().b200k_rope(ctypes.byref(a), _stream()))

@@ -345,6 +345,38 @@ at::Tensor log_softmax(const at::Tensor& x, int64_t dim, bool half_to_float) {
   return softmax_impl(x, dim, half_to_float, true);
 }
 
+// out = x * cos + rotate_half(x) * sin with cos / sin broadcast to x's shape;
+// out has x's shape, `out_stride` (the decomposed graph's layout) or dense.
+at::Tensor rope(const at::Tensor& x, const at::Tensor& cos, const at::Tensor& sin, at::IntArrayRef out_stride) {
+  TORCH_CHECK(x.is_cuda() && cos.is_cuda() && sin.is_cuda(), "b200::rope: CUDA tensors expected");
+  TORCH_CHECK(x.dim() >= 1 && x.dim() <= 4, "b200::rope: rank 1..4");
+  TORCH_CHECK(cos.scalar_type() == x.scalar_type() && sin.scalar_type() == x.scalar_type(),
+              "b200::rope: x, cos and sin of one dtype");
+  c10::cuda::CUDAGuard guard(x.device());
+  const at::Tensor c = cos.expand(x.sizes());
+  const at::Tensor s = sin.expand(x.sizes());
+  at::Tensor out = out_stride.empty() ? at::empty(x.sizes(), x.options())
+                                      : at::empty_strided(x.sizes(), out_stride, x.options());
+  B200kRopeArgs a;
+  std::memset(&a, 0, sizeof(a));
+  const int pad = 4 - static_cast<int>(x.dim());
+  for (int d = 0; d < 4; ++d) {
+    const bool real = d >= pad;
+    a.sizes[d] = real ? x.size(d - pad) : 1;
+    a.x_strides[d] = real ? x.stride(d - pad) : 0;
+    a.cos_strides[d] = real ? c.stride(d - pad) : 0;
+    a.sin_strides[d] = real ? s.stride(d - pad) : 0;
+    a.out_strides[d] = real ? out.stride(d - pad) : 0;
+  }
+  a.x = x.data_ptr();
+  a.cos = c.data_ptr();
+  a.sin = s.data_ptr();
+  a.out = out.data_ptr();
+  a.dtype = to_dt(x.scalar_type());
+  check(b200k_rope(&a, stream_of(x)), "rope");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(b200, m) {
@@ -361,6 +393,7 @@ TORCH_LIBRARY(b200, m) {
       "(Tensor, Tensor, Tensor)");
   m.def("softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("log_softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
+  m.def("rope(Tensor x, Tensor cos, Tensor sin, int[] out_stride=[]) -> Tensor");
   m.def("gemm_status(int device, bool reset) -> int", &gemm_status);
 }
 
@@ -372,5 +405,6 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("layer_norm", &layer_norm);
   m.impl("softmax", &softmax);
   m.impl("log_softmax", &log_softmax);
+  m.impl("rope", &rope);
 }
 
