@@ -66,6 +66,8 @@ def test_vit_block_stack_bf16():
     # proj+res, fc1+gelu, fc2+res per block; qkv (bias only, no pointwise tail) stays cuBLAS
     assert t.count("b200.gemm_epilogue.default") == 3 * 2
     assert "b200.layer_norm.default" in t
+    ops = [n.target for g in graphs for n in g.graph.nodes if n.op == "call_function"]
+    assert torch.ops.aten.convolution.default not in ops  # patch embedding lowered to a GEMM
     assert _rel(got, want) < 2e-2
 
 

@@ -386,3 +386,45 @@ def test_llama_layer_fuses_both_rotations():
     cos, sin = m.cos[:16].to(torch.bfloat16), m.sin[:16].to(torch.bfloat16)
     graphs = fused_graphs(layer, (x, cos, sin))
     assert sum(len(_rope_nodes(g)) for g in graphs) == 2
+
+
+class _Patch(nn.Module):
+    def __init__(self, bias=True):
+        super().__init__()
+        self.proj = nn.Conv2d(3, 32, 16, 16, bias=bias)
+
+    def forward(self, img):
+        return self.proj(img).flatten(2).transpose(1, 2)
+
+
+@pytest.mark.parametrize("bias", [True, False])
+def test_patchify_lowers_patch_conv_to_gemm(bias):
+    """A kernel == stride convolution becomes im2col + (add)mm with the
+    convolution's NCHW result layout; the rewritten graph computes the same
+    values as the convolution (run here on CPU in fp32 arithmetic)."""
+    torch.manual_seed(0)
+    model = _Patch(bias).to(torch.bfloat16)
+    img = torch.randn(2, 3, 64, 64).to(torch.bfloat16)
+    (gm,) = fused_graphs(model, (img,))
+    targets = [n.target for n in gm.graph.nodes if n.op == "call_function"]
+    assert torch.ops.aten.convolution.default not in targets
+    assert (torch.ops.aten.addmm.default if bias else torch.ops.aten.mm.default) in targets
+    # numerics of the lowering itself: conv2d == im2col @ w^T (+ b), fp32 on CPU
+    x, w = img.float(), model.proj.weight.float()
+    p = x.view(2, 3, 4, 16, 4, 16).permute(0, 2, 4, 1, 3, 5).reshape(32, 768)
+    y = p @ w.view(32, 768).t() + (model.proj.bias.float() if bias else 0)
+    ref = torch.nn.functional.conv2d(x, w, model.proj.bias.float() if bias else None, stride=16)
+    torch.testing.assert_close(y.view(2, 4, 4, 32).permute(0, 3, 1, 2), ref, rtol=1e-4, atol=1e-4)
+
+
+def test_patchify_leaves_overlapping_convolutions():
+    class Conv(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.c = nn.Conv2d(3, 8, 3, 1, padding=1)
+
+        def forward(self, x):
+            return self.c(x)
+
+    (gm,) = fused_graphs(Conv().to(torch.bfloat16), (torch.randn(1, 3, 16, 16).to(torch.bfloat16),))
+    assert torch.ops.aten.convolution.default in [n.target for n in gm.graph.nodes if n.op == "call_function"]

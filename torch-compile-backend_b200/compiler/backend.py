@@ -20,6 +20,7 @@ from torch._functorch.aot_autograd import make_boxed_func
 from compiler import runtime
 from compiler.optimization import config
 from compiler.optimization.fusion_epilogue import fuse_epilogue
+from compiler.optimization.fusion_patchify import fuse_patchify
 from compiler.optimization.fusion_pointwise import fuse_pointwise
 from compiler.optimization.fusion_rope import fuse_rope
 from compiler.optimization.fusion_rowreduce import fuse_rowreduce
@@ -37,6 +38,8 @@ def _dump(gm: fx.GraphModule) -> None:
 
 
 def compiler(gm: fx.GraphModule, example_inputs):
+    if config.EXTENSIONS and config.ENABLE_PATCHIFY:
+        gm = fuse_patchify(gm)  # patch-embedding convolutions -> im2col + addmm (extension)
     if config.EXTENSIONS and config.ENABLE_ROWREDUCE:
         gm = fuse_rowreduce(gm)  # whole row groups (extension; runs first so the
         #                          pointwise passes do not split them)

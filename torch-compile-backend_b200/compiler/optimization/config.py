@@ -2,11 +2,13 @@
 
 Environment flags (read once at import, overridable as module attributes):
   B200_EXTENSIONS=0   reference-identical grouping only: no view look-through
-                      for 3-d linears, no row-reduction or rotary-embedding fusion
+                      for 3-d linears, no row-reduction or rotary-embedding
+                      fusion, no patch-embedding lowering
   B200_EPILOGUE=0     skip the GEMM+epilogue pass
   B200_POINTWISE=0    skip the pointwise pass
   B200_ROWREDUCE=0    skip the row-reduction pass
   B200_ROPE=0         skip the rotary-embedding pass
+  B200_PATCHIFY=0     keep patch-embedding convolutions as convolutions
   B200_DUMP=1         print each compiled graph and the fused-kernel programs
   B200_FAST_EPILOGUE=0  always interpret GEMM epilogue programs
 
@@ -32,6 +34,7 @@ ENABLE_EPILOGUE = _flag("B200_EPILOGUE", True)
 ENABLE_POINTWISE = _flag("B200_POINTWISE", True)
 ENABLE_ROWREDUCE = _flag("B200_ROWREDUCE", True)
 ENABLE_ROPE = _flag("B200_ROPE", True)
+ENABLE_PATCHIFY = _flag("B200_PATCHIFY", True)
 DUMP = _flag("B200_DUMP", False)
 FAST_EPILOGUE = _flag("B200_FAST_EPILOGUE", True)  # compiled path for canonical GEMM epilogues
 
