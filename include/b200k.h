@@ -243,9 +243,11 @@ int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 #define B200K_NOALLOC_STATUS_BYTES 4
 int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream);
 
-/* Number of GEMM tile configurations in the built-in table and their shapes.
- * Config 2 (128 x 192 tiles) runs compiled epilogues only: a call forcing it
- * whose epilogue is interpreted runs config 0 instead. */
+/* Number of GEMM tile configurations in the built-in table and their shapes
+ * (block_m x block_n).  Config 2 (128 x 192 tiles) runs compiled epilogues
+ * only; config 3 (256 x 256 tiles, each computed by a cluster of two CTAs on
+ * two SMs) runs compiled epilogues with K-major B and 16-bit output only.  A
+ * call forcing either outside its domain runs config 0 instead. */
 int b200k_gemm_num_configs(void);
 int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages);
 /* The configuration b200k_gemm_epilogue picks for a problem with a compiled

@@ -145,14 +145,14 @@ def test_gemm_sweep_configs(shape, act, path):
 
 @pytest.mark.parametrize("M,N,K", [(1, 8, 8), (37, 72, 24), (128, 256, 64), (130, 260, 72), (300, 100, 136),
                                    (257, 1000, 768), (64, 4096, 1024)])
-@pytest.mark.parametrize("config", [0, 1, 2])
+@pytest.mark.parametrize("config", [0, 1, 2, 3])
 @pytest.mark.parametrize("ab", ["bfloat16", "float16"])
 @pytest.mark.parametrize("path", ["compiled", "interpreted"])
 def test_gemm_edge_shapes(M, N, K, config, ab, path):
     """Ragged M/N/K (partial tiles, K tail inside a 64-wide block, M < 128,
     N whose rows are not 16-byte multiples -> direct-store path), every tile
-    config (an interpreted epilogue forced to 192-wide tiles runs 256-wide
-    ones), both operand dtypes,
+    config (an interpreted epilogue forced to 192-wide or CTA-pair tiles
+    runs 256-wide ones), both operand dtypes,
     gelu-tanh + bias + residual."""
     dt = _tdt(ab)
     g = torch.Generator(device=DEV).manual_seed(M * 7 + N)
@@ -169,6 +169,36 @@ def test_gemm_edge_shapes(M, N, K, config, ab, path):
     want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
                                 [b.float().cpu().numpy(), r.float().cpu().numpy()], ab, bias=b.float().cpu().numpy())
     _assert_close(out, want, *_gemm_tol(want))
+
+
+@pytest.mark.parametrize("act", ["none", "gelu", "silu"])
+@pytest.mark.parametrize("shape", [(256, 256, 64), (4096, 4096, 4096), (2000, 3000, 1600), (300, 520, 2048)])
+def test_gemm_pair_tiles_equal_single_cta_tiles(act, shape):
+    """256 x 256 tiles on CTA pairs (config 3, tcgen05 cta_group::2) against
+    128 x 256 tiles on single CTAs (config 0): the same MMAs over the same K
+    order and the same epilogue, so the outputs are equal bit for bit, full
+    and ragged tiles alike; and the fp32 oracle agrees on sampled rows."""
+    M, N, K = shape
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    x = (0.02 * torch.randn(M, K, device=DEV, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn(N, K, device=DEV, generator=g)).to(torch.bfloat16)
+    b = (0.01 * torch.randn(N, device=DEV, generator=g)).to(torch.bfloat16)
+    r = (0.02 * torch.randn(M, N, device=DEV, generator=g)).to(torch.bfloat16)
+    code, imm, spec, form = epilogue_program(act, residual=True)
+    outs = []
+    for cfg in (3, 0):
+        out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+        status = torch.zeros(1, dtype=torch.int32, device=DEV)
+        cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=cfg, status=status, form=form)
+        torch.cuda.synchronize()
+        assert status.item() == 0
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    rows = torch.arange(0, M, max(1, M // 64), device=DEV)
+    want = oracle.gemm_epilogue(x[rows].float().cpu().numpy(), w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), r[rows].float().cpu().numpy()], "bfloat16",
+                                bias=b.float().cpu().numpy())
+    _assert_close(outs[0][rows], want, *_gemm_tol(want))
 
 
 def test_gemm_192_tiles_with_interpreted_epilogue_run_config_0():
@@ -207,7 +237,7 @@ def role_program(act: str, role: str, round_to: str | None):
 @pytest.mark.parametrize("act", ["none", "silu", "gelu"])
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
 @pytest.mark.parametrize("rounded", [True, False])
-@pytest.mark.parametrize("config", [0, 1, 2])
+@pytest.mark.parametrize("config", [0, 1, 2, 3])
 def test_gemm_row_operand_roles(role, act, dt, rounded, config):
     """A full 16-bit matrix as residual or scale, after an activation that is
     (rounded) or is not rounded to the output type first.  Rounded, the
@@ -229,7 +259,7 @@ def test_gemm_row_operand_roles(role, act, dt, rounded, config):
     for path in ("compiled", "interpreted"):
         out = torch.empty(M, N, device=DEV, dtype=t)
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
-        cfg = 0 if (config == 2 and path == "interpreted") else config  # 192-wide: compiled only
+        cfg = 0 if (config >= 2 and path == "interpreted") else config  # 192-wide, pairs: compiled only
         cabi.gemm_epilogue(x, w.t(), [b, m], code, imm, out, tile_config=cfg, status=status,
                            form=form if path == "compiled" else None)
         torch.cuda.synchronize()

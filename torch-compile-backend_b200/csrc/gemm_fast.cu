@@ -7,11 +7,29 @@
 #include "gemm_kernel.cuh"
 
 #if !defined(B200K_FAST_BN) || !defined(B200K_FAST_ACT)
-#error "compile with -DB200K_FAST_BN=<256|192|128> -DB200K_FAST_ACT=<activation>"
+#error "compile with -DB200K_FAST_BN=<256|192|128|2> -DB200K_FAST_ACT=<activation> (2: the CTA-pair kernels)"
 #endif
 
 namespace b200k {
 namespace gemm {
+
+#if B200K_FAST_BN == 2
+// CTA-pair kernels: 256 x 256 tiles on two-CTA clusters, 16-bit output.
+#define B200K_PAIR_FN2(ACT) launch_pair_##ACT
+#define B200K_PAIR_FN(ACT) B200K_PAIR_FN2(ACT)
+int B200K_PAIR_FN(B200K_FAST_ACT)(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                                  const Params& p, int grid, cudaStream_t st) {
+  constexpr int kAct = B200K_FAST_ACT;
+  switch (row) {
+    case ROW_NONE: return launch_pair<kPairStages, 2, kAct, ROW_NONE>(ta, tb, to, p, grid, st);
+    case ROW_SCALE: return launch_pair<kPairStages, 2, kAct, ROW_SCALE>(ta, tb, to, p, grid, st);
+    case ROW_RES: return launch_pair<kPairStages, 2, kAct, ROW_RES>(ta, tb, to, p, grid, st);
+    case ROW_SCALE_PK: return launch_pair<kPairStages, 2, kAct, ROW_SCALE_PK>(ta, tb, to, p, grid, st);
+    case ROW_RES_PK: return launch_pair<kPairStages, 2, kAct, ROW_RES_PK>(ta, tb, to, p, grid, st);
+    default: return B200K_ERR_UNSUPPORTED;
+  }
+}
+#else
 namespace {
 
 constexpr int config_of(int bn) {
@@ -51,6 +69,7 @@ int B200K_FAST_FN(B200K_FAST_BN, B200K_FAST_ACT)(bool bnm, int ob, int row, cons
     return launch_one<kBN, kStages, false, 4, true, kAct, ROW_NONE>(ta, tb, to, p, grid, st);
   return B200K_ERR_UNSUPPORTED;
 }
+#endif
 
 }  // namespace gemm
 }  // namespace b200k

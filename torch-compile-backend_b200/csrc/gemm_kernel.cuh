@@ -180,6 +180,63 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo, uin
   return d;
 }
 
+// ------------------------------------------------ CTA-pair (cta_group::2) forms
+// A cluster of two CTAs on two SMs computes one 256-row tile: each CTA holds
+// its own 128 rows of A and one half of the tile's B columns in its shared
+// memory (same offsets in both), and the even CTA issues M = 256 MMAs that
+// read both CTAs' halves and write each CTA's 128 accumulator rows into that
+// CTA's TMEM.  None of these forms multicasts a load.
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared-memory offset in CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+__device__ __forceinline__ void umma_f16_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on the barrier at shared::cluster address `bar` (this CTA's or the
+// peer's) when every pair MMA this thread issued so far has completed.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+// Tile load into this CTA's shared memory whose byte count completes on the
+// barrier at shared::cluster address `bar` (the even CTA's).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
 // ------------------------------------------------------------- bounded waits
 struct Ctl {
   volatile int* abort;
@@ -397,8 +454,7 @@ template <int ACT>
 __device__ __forceinline__ void apply_act8(float (&v)[8]) {
   if constexpr (ACT == B200K_ACT_GELU_ERF) {
     gelu_erf_as8(v);
-    return;
-  }
+  } else {
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float x = v[j];
@@ -414,6 +470,7 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
     } else if constexpr (ACT == B200K_ACT_TANH) {
       v[j] = op_tanh(x);
     }
+  }
   }
 }
 
@@ -638,39 +695,46 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
   }
 }
 
-template <int BN, int OUT_BYTES, int ACT, int ROW>
+// PAIR: the tiles are 256 x BN, one per CTA pair (the grid's cluster index
+// walks them), and this CTA's 128 rows start at `rank` x 128; the
+// accumulator is released on the even CTA's barrier (`tempty_even`).
+template <int BN, int OUT_BYTES, int ACT, int ROW, bool PAIR = false>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
                                                    uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
-                                                   int cg, int lane, const Ctl& ctl) {
+                                                   int cg, int lane, const Ctl& ctl, uint32_t rank = 0) {
   constexpr int CW = Epi<BN>::CW;
   constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and tile
+  constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile
+  const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int rank_rows = static_cast<int>(rank) * BM;
   FastOps cur{}, nxt{};
-  if (static_cast<int>(blockIdx.x) < p.num_tiles) {
+  if (t0 < p.num_tiles) {
     int tm, tn;
-    tile_coords(blockIdx.x, p, tm, tn);
-    prefetch_row16_l2<CW, ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + cg * CW);
-    fast_prefetch<ROW>(p, tm * BM + quarter * 32 + lane, tn * BN + cg * CW, lane, cur);
+    tile_coords(t0, p, tm, tn);
+    prefetch_row16_l2<CW, ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW);
+    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW, lane, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
   const bool stamper = quarter == 0 && cg == 0 && lane == 0;
   int ti = 0;
-  for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++ti) {
+  for (int t = t0; t < p.num_tiles; t += step, ++ti) {
     int tm, tn;
     tile_coords(t, p, tm, tn);
-    const bool more = t + static_cast<int>(gridDim.x) < p.num_tiles;
+    const bool more = t + step < p.num_tiles;
     int m2 = 0, n2 = 0;
     if (more) {
       int tm2, tn2;
-      tile_coords(t + gridDim.x, p, tm2, tn2);
-      m2 = tm2 * BM + quarter * 32 + lane;
+      tile_coords(t + step, p, tm2, tn2);
+      m2 = tm2 * TM + rank_rows + quarter * 32 + lane;
       n2 = tn2 * BN + cg * CW;
       prefetch_row16_l2<CW, ROW>(p, m2, n2);
     }
     if (!wait_bar(&tfull[acc], aph, ctl)) break;
     tc_fence_after();
     if (stamper) stamp_tile(p, ti, 4);
-    const int row0 = tm * BM + quarter * 32;
+    const int row0 = tm * TM + rank_rows + quarter * 32;
     const int m = row0 + lane;
     const int n0 = tn * BN + cg * CW;
     const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
@@ -687,7 +751,10 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
     if (stamper) stamp_tile(p, ti, 5);
     tc_fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&tempty[acc]);
+    if (lane == 0) {
+      if (PAIR && rank != 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+      else mbar_arrive(&tempty[acc]);
+    }
     if (++acc == 2) {
       acc = 0;
       aph ^= 1u;
@@ -927,11 +994,220 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
   }
 }
 
-struct TileConfig {
-  int bn, stages;
+// ------------------------------------------------------------ CTA-pair kernel
+// 256 x 256 tiles on a cluster of two CTAs (compiled epilogues, K-major B).
+// Per CTA: a STAGES-deep ring of its own 128 A rows and its half (128 rows)
+// of the tile's B rows (32 KB a stage instead of 48 KB for one CTA's 128 x
+// 256 tile: the pair shares B), two 256-column accumulators allocated as a
+// pair, and eight epilogue warps on its own 128 rows.  Barriers: full[s] and
+// tempty[a] live in the even CTA (the odd CTA's loads and epilogue complete
+// and arrive there); empty[s] and tfull[a] in both CTAs (the even CTA's MMA
+// thread commits to each copy).  Every wait is bounded as in the one-CTA
+// kernel; cluster barriers open and close the kernel so that no CTA leaves
+// while the other may still signal one of its barriers.
+constexpr int kPairBN = 256;
+template <int STAGES, int OUT_BYTES>
+struct PairCfg {
+  static constexpr uint32_t kABytes = BM * BK * 2;
+  static constexpr uint32_t kBBytes = (kPairBN / 2) * BK * 2;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<kPairBN>::kWarps * kStgBytes;
+  static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
+  static_assert(kSmem <= 232448, "shared memory budget");
+  static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
 };
-// Config 2 (192-wide tiles, twelve epilogue warps) exists for compiled epilogues only.
-constexpr TileConfig kConfigs[] = {{256, 4}, {128, 6}, {192, 4}};
+
+template <int STAGES, int OUT_BYTES, int ACT, int ROW>
+__global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
+  using C = PairCfg<STAGES, OUT_BYTES>;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sbase = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* sA = sbase;
+  uint8_t* sB = sA + STAGES * C::kABytes;
+  uint8_t* sStg = sB + STAGES * C::kBBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sbase + C::kBarOff);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_rank();
+  const bool even = rank == 0;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) stamp(p, 0);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * Epi<kPairBN>::kWarps);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&tmA);
+    prefetch_map(&tmB);
+    prefetch_map(&tmO);
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, C::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs: barriers initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const Ctl ctl{abort_flag, p.status, static_cast<uint64_t>(p.timeout_ns)};
+  const int cid = static_cast<int>(blockIdx.x >> 1);
+  const int ncl = static_cast<int>(gridDim.x >> 1);
+  if (threadIdx.x == 0) stamp(p, 1);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0;
+      int64_t issued = 0;
+      bool ok = true;
+      int ti = 0;
+      constexpr uint32_t kTx = 2 * (C::kABytes + C::kBBytes);  // both CTAs' loads of a stage
+      for (int t = cid; t < p.num_tiles && ok; t += ncl, ++ti) {
+        int tm, tn;
+        tile_coords(t, p, tm, tn);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&empty[s], ph ^ 1u, ctl)) {
+            ok = false;
+            break;
+          }
+          if (kb == 0) stamp_tile(p, ti, 0);
+          if (kb == p.k_blocks - 1) stamp_tile(p, ti, 1);
+          const uint32_t fb = cluster_addr(&full[s], 0);
+          if (even) mbar_arrive_expect_tx(&full[s], kTx);
+          tma_load_2d_pair(sA + s * C::kABytes, &tmA, fb, kb * BK, tm * (2 * BM) + static_cast<int>(rank) * BM);
+          tma_load_2d_pair(sB + s * C::kBBytes, &tmB, fb, kb * BK,
+                           tn * kPairBN + static_cast<int>(rank) * (kPairBN / 2));
+          ++issued;
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // Tail: wait until the MMA has released every stage this CTA filled, so
+      // that no commit of the even CTA targets this CTA's barriers after the
+      // closing cluster barrier.
+      for (int x = 0; x < STAGES; ++x)
+        if (issued > x) wait_bar_drain(&empty[x], x < s ? ph : (ph ^ 1u), 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    if (even && lane == 0) {
+      int s = 0, acc = 0;
+      uint32_t ph = 0, aph = 0;
+      bool ok = true;
+      int ti = 0;
+      for (int t = cid; t < p.num_tiles && ok; t += ncl, ++ti) {
+        if (!wait_bar(&tempty[acc], aph ^ 1u, ctl)) break;
+        tc_fence_after();
+        stamp_tile(p, ti, 2);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairBN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!wait_bar(&full[s], ph, ctl)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(sA + s * C::kABytes);
+          const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
+#pragma unroll
+          for (int k = 0; k < BK / UMMA_K; ++k)
+            umma_f16_pair(d_tmem, sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024),
+                          sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024), p.idesc, (kb | k) != 0 ? 1u : 0u);
+          umma_commit_pair(smem_u32(&empty[s]));
+          umma_commit_pair(cluster_addr(&empty[s], 1));
+          if (++s == STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        umma_commit_pair(cluster_addr(&tfull[acc], 1));
+        stamp_tile(p, ti, 3);
+        if (++acc == 2) {
+          acc = 0;
+          aph ^= 1u;
+        }
+      }
+      // Every MMA this thread issued completes before TMEM can be released.
+      umma_commit_pair(smem_u32(drain));
+      wait_bar_drain(drain, 0, 100000000ull);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int ew = warp - 4;
+    epilogue_fast_loop<kPairBN, OUT_BYTES, ACT, ROW, true>(p, &tmO, tmem_base, tfull, tempty,
+                                                          sStg + ew * kStgBytes, warp & 3, ew >> 2, lane, ctl, rank);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the other can still signal its barriers
+  if (threadIdx.x == 0) stamp(p, 2);
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, C::kTmemCols);
+  }
+}
+
+template <int STAGES, int OB, int ACT, int ROW>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
+                cudaStream_t st) {
+  using C = PairCfg<STAGES, OB>;
+  auto kern = gemm_pair_kernel<STAGES, OB, ACT, ROW>;
+  static bool attr_set = false;  // per instantiation; idempotent
+  if (!attr_set) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
+      return B200K_ERR_LAUNCH;
+    attr_set = true;
+  }
+  cudaLaunchConfig_t cfg;
+  std::memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3(Epi<kPairBN>::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, ta, tb, to, p) != cudaSuccess) return B200K_ERR_LAUNCH;
+  return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
+}
+
+struct TileConfig {
+  int bm, bn, stages;  // bm 256: a CTA pair per tile
+};
+// Config 2 (192-wide tiles, twelve epilogue warps) and config 3 (256 x 256
+// tiles on CTA pairs) exist for compiled epilogues only; config 3 also needs
+// K-major B and 16-bit output.
+constexpr TileConfig kConfigs[] = {{128, 256, 4}, {128, 128, 6}, {128, 192, 4}, {256, 256, 6}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
 template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW>
@@ -976,6 +1252,17 @@ B200K_DECLARE_FAST(192, 2)
 B200K_DECLARE_FAST(192, 3)
 B200K_DECLARE_FAST(192, 4)
 #undef B200K_DECLARE_FAST
+// CTA-pair kernels (256 x 256 tiles, K-major B, 16-bit output, every row role).
+#define B200K_DECLARE_PAIR(ACT)                                                                                   \
+  int launch_pair_##ACT(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, \
+                        int grid, cudaStream_t st);
+B200K_DECLARE_PAIR(0)
+B200K_DECLARE_PAIR(1)
+B200K_DECLARE_PAIR(2)
+B200K_DECLARE_PAIR(3)
+B200K_DECLARE_PAIR(4)
+#undef B200K_DECLARE_PAIR
+constexpr int kPairStages = 6;
 
 }  // namespace gemm
 }  // namespace b200k

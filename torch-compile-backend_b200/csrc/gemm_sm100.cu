@@ -81,7 +81,7 @@ int launch_fast(int bn, int act, bool bnm, int ob, int row, const CUtensorMap& t
   return B200K_ERR_UNSUPPORTED;
 }
 
-int pick(int64_t M, int64_t N, int sms, bool compiled) {
+int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) {
   // Per-SM time of a config ~ (tiles per SM, rounded up) x (tile width) x
   // (cost per column).  Measured on B200 (bias + residual epilogue, 4096^3):
   // 128x256 tiles, 4 waves: 0.134 ms; 128x128 tiles, 7 waves: 0.173 ms, i.e.
@@ -90,22 +90,42 @@ int pick(int64_t M, int64_t N, int sms, bool compiled) {
   // 192-wide tile (compiled epilogues only) spreads its epilogue over twelve
   // warps and loses little per column; it wins where 256-wide tiles leave a
   // mostly idle last wave (N = 768: 297 tiles on 148 SMs = 3 waves, against
-  // 396 tiles of 3/4 the work = 3 shorter waves).
+  // 396 tiles of 3/4 the work = 3 shorter waves).  A CTA pair's 256 x 256
+  // tile gives each SM the work of one 128 x 256 tile with a third less
+  // operand traffic per FLOP (the pair shares B): measured 8-15 % faster
+  // from K = 2048 up (4096^3 1148 -> 1321 TFLOP/s, 16384 x 4096 x 14336 with
+  // GELU 1342 -> 1502), no faster at K = 768, where the epilogue bounds a tile
+  // and the 192-wide tile's twelve epilogue warps win; pairs need K >= 1536.
+  pair_ok = pair_ok && K >= 1536;
   int best = 0;
   double best_cost = 1e300;
   for (int c = 0; c < kNumConfigs; ++c) {
-    const int bn = kConfigs[c].bn;
-    if (bn == 192 && !compiled) continue;
-    const int64_t tiles = ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
-    const int64_t per_sm = (tiles + sms - 1) / sms;
-    const double per_col = bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5);
-    const double cost = static_cast<double>(per_sm) * bn * per_col;
+    const int bm = kConfigs[c].bm, bn = kConfigs[c].bn;
+    const bool pair = bm == 2 * BM;
+    if ((bn == 192 && !compiled) || (pair && !pair_ok)) continue;
+    const int64_t tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
+    const int64_t slots = pair ? sms / 2 : sms;  // tiles that run at once
+    const int64_t waves = (tiles + slots - 1) / slots;
+    const double per_col = pair ? 0.9 : (bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5));
+    const double cost = static_cast<double>(waves) * bn * per_col;
     if (cost < best_cost) {
       best_cost = cost;
       best = c;
     }
   }
   return best;
+}
+
+int launch_pair(int act, int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+                const Params& p, int grid, cudaStream_t st) {
+  switch (act) {
+    case 0: return launch_pair_0(row, ta, tb, to, p, grid, st);
+    case 1: return launch_pair_1(row, ta, tb, to, p, grid, st);
+    case 2: return launch_pair_2(row, ta, tb, to, p, grid, st);
+    case 3: return launch_pair_3(row, ta, tb, to, p, grid, st);
+    case 4: return launch_pair_4(row, ta, tb, to, p, grid, st);
+    default: return B200K_ERR_UNSUPPORTED;
+  }
 }
 
 }  // namespace gemm
@@ -130,7 +150,7 @@ extern "C" int b200k_gemm_num_configs(void) { return kNumConfigs; }
 
 extern "C" int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages) {
   if (config < 0 || config >= kNumConfigs) return B200K_ERR_ARG;
-  if (block_m) *block_m = BM;
+  if (block_m) *block_m = kConfigs[config].bm;
   if (block_n) *block_n = kConfigs[config].bn;
   if (block_k) *block_k = BK;
   if (stages) *stages = kConfigs[config].stages;
@@ -138,10 +158,9 @@ extern "C" int b200k_gemm_config_info(int config, int* block_m, int* block_n, in
 }
 
 extern "C" int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K) {
-  (void)K;
   int sms = device_sm_count();
   if (sms <= 0) sms = 148;
-  return pick(M, N, sms, true);
+  return pick(M, N, K, sms, true, true);
 }
 
 extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
@@ -207,20 +226,25 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
                     (bias_mode == XM_NONE || bias_mode == XM_BCAST);
 
+  const bool pair_ok = fast && !bnm && ob == 2;  // the CTA-pair kernels' domain
+
   const int sms = device_sm_count();
   if (sms <= 0) return B200K_ERR_DEVICE;
   int cfg = a->tile_config;
-  if (cfg < 0) cfg = pick(a->M, a->N, sms, fast);
+  if (cfg < 0) cfg = pick(a->M, a->N, a->K, sms, fast, pair_ok);
   if (cfg >= kNumConfigs) return B200K_ERR_ARG;
   if (kConfigs[cfg].bn == 192 && !fast) cfg = 0;  // 192-wide tiles run compiled epilogues only
+  if (kConfigs[cfg].bm == 2 * BM && !pair_ok) cfg = 0;
   const int bn = kConfigs[cfg].bn;
+  const int bm = kConfigs[cfg].bm;
+  const bool pair = bm == 2 * BM;
 
   Params p;
   std::memset(&p, 0, sizeof(p));
   p.M = static_cast<int32_t>(a->M);
   p.N = static_cast<int32_t>(a->N);
   p.K = static_cast<int32_t>(a->K);
-  p.tiles_m = static_cast<int32_t>((a->M + BM - 1) / BM);
+  p.tiles_m = static_cast<int32_t>((a->M + bm - 1) / bm);
   p.tiles_n = static_cast<int32_t>((a->N + bn - 1) / bn);
   const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffff) return B200K_ERR_SHAPE;
@@ -234,7 +258,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 2000000000ll;
   const uint32_t fmt = a->ab_dtype == B200K_BF16 ? 1u : 0u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
-            (static_cast<uint32_t>(BM >> 4) << 24);
+            (static_cast<uint32_t>(bm >> 4) << 24);
   for (int i = 0; i < a->n_extras; ++i) {
     const B200kEpiOperand& e = a->extras[i];
     EpiOperand& q = p.ex[i];
@@ -265,13 +289,16 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (bnm) {
     if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * 2, 64, BK)) return B200K_ERR_LAUNCH;
   } else {
-    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, bn)) return B200K_ERR_LAUNCH;
+    // a CTA of a pair loads its half of the tile's B rows
+    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, pair ? bn / 2 : bn))
+      return B200K_ERR_LAUNCH;
   }
   p.direct_store = tma_out ? 0 : 1;
   if (tma_out) {
     if (!make_map(&to, a->out_dtype, a->out, a->N, a->M, a->out_stride_m * ob, 128 / ob, 32)) return B200K_ERR_LAUNCH;
   }
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, sms));
+  const int grid = pair ? 2 * static_cast<int>(std::min<int64_t>(tiles, sms / 2))
+                        : static_cast<int>(std::min<int64_t>(tiles, sms));
   if (a->trace && a->trace_words >= static_cast<int64_t>(grid) * B200K_GEMM_TRACE_WORDS)
     p.trace = reinterpret_cast<unsigned long long*>(a->trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
@@ -285,6 +312,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     } else if (a->form.round == a->out_dtype) {
       p.f_round = -1;  // the store's own rounding is the same one
     }
+    if (pair) return launch_pair(a->form.act, row, ta, tb, to, p, grid, st);
     return launch_fast(bn, a->form.act, bnm, ob, row, ta, tb, to, p, grid, st);
   }
   if (cfg == 0) return launch_interp<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
