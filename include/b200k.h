@@ -207,7 +207,7 @@ typedef struct {
   int32_t* status;     /* optional device word: set to B200K_ERR_TIMEOUT by a stuck wait */
   int64_t timeout_ns;  /* 0 = default (2 s) */
   B200kEpilogueForm form;
-  int32_t pad2;
+  int32_t test_flags;  /* 0, or B200K_GEMM_TEST_* hooks for failure-detection tests */
   /* Optional diagnostic timeline (NULL = off): per CTA, B200K_GEMM_TRACE_WORDS
    * global-timer stamps (ns) -- [0] entry, [1] set-up done, [2] exit, then per
    * tile i < 40 at 8 + 6*i: first and last TMA issue, MMA start, last MMA
@@ -219,6 +219,13 @@ typedef struct {
   int64_t trace_words;
 } B200kGemmArgs;
 #define B200K_GEMM_TRACE_WORDS 256
+/* Test hook (test_flags bit): the MMA thread does not signal the first tile's
+ * accumulator as ready, so the epilogue's wait on it runs out after
+ * timeout_ns.  The kernel then takes its timeout path -- status word set to
+ * B200K_ERR_TIMEOUT, every role leaves its loop, in-flight copies and MMAs
+ * drain, TMEM is freed -- and returns; no fault, the context stays usable.
+ * Never set outside failure-detection tests. */
+#define B200K_GEMM_TEST_WITHHOLD_READY 1
 
 int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 

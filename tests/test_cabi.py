@@ -82,7 +82,7 @@ STRUCTS = {
     "B200kPointwiseArgs": (cabi.PointwiseArgs, ["rank", "n_inputs", "sizes", "inputs", "out", "out_dtype", "program"]),
     "B200kEpiOperand": (cabi.EpiOperand, ["ptr", "dtype", "stride_m", "stride_n"]),
     "B200kGemmArgs": (cabi.GemmArgs, ["M", "a", "b_stride_n", "ab_dtype", "out", "n_extras", "tile_config",
-                                      "extras", "program", "status", "timeout_ns", "form", "trace",
+                                      "extras", "program", "status", "timeout_ns", "form", "test_flags", "trace",
                                       "trace_words"]),
     "B200kEpilogueForm": (cabi.EpilogueForm, ["kind", "bias", "act", "round", "scale", "residual"]),
     "B200kRowNormArgs": (cabi.RowNormArgs, ["rows", "x", "kind", "weight", "flags", "bias", "eps", "out",

@@ -510,3 +510,34 @@ def test_rope_matches_eager_bit_for_bit(dtype, case):
     # and through the torch op with the decomposed graph's layout
     got = torch.ops.b200.rope(x, c, s, list(want.stride()))
     assert got.stride() == want.stride() and torch.equal(got, want)
+
+
+# ------------------------------------------------------------- failure detection
+@pytest.mark.parametrize("config", [0, 3])
+def test_gemm_stalled_wait_times_out_and_context_survives(config):
+    """A wait that nothing completes (the test hook withholds the first
+    tile's accumulator-ready signal) runs out after the 50 ms limit: the
+    kernel reports B200K_ERR_TIMEOUT in the status word, drains, frees TMEM
+    and returns -- on the one-CTA kernel and on the CTA-pair kernel -- and the
+    same context then computes a correct GEMM."""
+    M, N, K = 1024, 1024, 2048
+    g = torch.Generator(device=DEV).manual_seed(9)
+    x = (0.02 * torch.randn(M, K, device=DEV, generator=g)).to(torch.bfloat16)
+    w = (0.02 * torch.randn(N, K, device=DEV, generator=g)).to(torch.bfloat16)
+    b = (0.01 * torch.randn(N, device=DEV, generator=g)).to(torch.bfloat16)
+    r = (0.02 * torch.randn(M, N, device=DEV, generator=g)).to(torch.bfloat16)
+    code, imm, spec, form = epilogue_program("gelu", residual=True)
+    out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=config, status=status,
+                       timeout_ns=50_000_000, form=form, test_flags=cabi.GEMM_TEST_WITHHOLD_READY)
+    torch.cuda.synchronize()
+    assert status.item() == 6  # B200K_ERR_TIMEOUT
+    status.zero_()
+    cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=config, status=status, form=form)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    want = oracle.gemm_epilogue(x[:64].float().cpu().numpy(), w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), r[:64].float().cpu().numpy()], "bfloat16",
+                                bias=b.float().cpu().numpy())
+    _assert_close(out[:64], want, *_gemm_tol(want))

@@ -24,6 +24,7 @@ DTYPE = {
     torch.int32: I32, torch.int64: I64, torch.bool: BOOL, torch.uint8: U8,
 }
 ROW_RMSNORM, ROW_LAYERNORM, ROW_RMSNORM_SWIGLU = 0, 1, 2
+GEMM_TEST_WITHHOLD_READY = 1  # include/b200k.h: failure-detection test hook
 
 EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
@@ -70,7 +71,7 @@ class GemmArgs(ctypes.Structure):
                 ("n_extras", ctypes.c_int32), ("tile_config", ctypes.c_int32),
                 ("extras", EpiOperand * (MAX_INPUTS - 1)), ("program", Program),
                 ("status", ctypes.c_void_p), ("timeout_ns", ctypes.c_int64), ("form", EpilogueForm),
-                ("pad2", ctypes.c_int32), ("trace", ctypes.c_void_p), ("trace_words", ctypes.c_int64)]
+                ("test_flags", ctypes.c_int32), ("trace", ctypes.c_void_p), ("trace_words", ctypes.c_int64)]
 
 TRACE_WORDS = 256
 
@@ -175,7 +176,7 @@ def pointwise(inputs: list[torch.Tensor], code, imm, out: torch.Tensor) -> None:
 
 def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], code, imm, out: torch.Tensor,
                   tile_config: int = -1, status: torch.Tensor | None = None, timeout_ns: int = 0,
-                  form=None, noalloc: bool = False, trace: torch.Tensor | None = None) -> None:
+                  form=None, noalloc: bool = False, trace: torch.Tensor | None = None, test_flags: int = 0) -> None:
     """out[M,N] = program(a @ b, extras) with extras given as [M,N]-broadcastable tensors.
     noalloc=True calls b200k_gemm_epilogue_noalloc, which ignores `status` and
     uses the library's own status scratch (for hosts that cannot allocate)."""
@@ -199,6 +200,7 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
     g.program = make_program(code, imm)
     g.status = status.data_ptr() if status is not None else None
     g.timeout_ns = timeout_ns
+    g.test_flags = test_flags
     if form:
         (g.form.kind, g.form.bias, g.form.act, g.form.round, g.form.scale, g.form.residual) = form
     if trace is not None:  # int64 device tensor, TRACE_WORDS per CTA

@@ -86,7 +86,7 @@ struct Params {
   int32_t f_bias, f_act, f_round, f_scale, f_res;  // canonical epilogue form (fast path)
   int32_t xm_bias, xm_scale, xm_res;               // how the fast path stages each operand (XM_*)
   int32_t row_idx;                                 // extras index of the fast path's full-matrix operand
-  int32_t pad2;
+  int32_t test_flags;                              // B200K_GEMM_TEST_* hooks (0 in production)
   unsigned long long* trace;                       // diagnostic timeline, null = off
   EpiOperand ex[B200K_MAX_INPUTS - 1];
   B200kProgram prog;
@@ -908,7 +908,7 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if (!(ti == 0 && (p.test_flags & B200K_GEMM_TEST_WITHHOLD_READY))) umma_commit(&tfull[acc]);
         stamp_tile(p, ti, 3);
         if (++acc == 2) {
           acc = 0;
@@ -1143,8 +1143,10 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
           }
         }
         if (!ok) break;
-        umma_commit_pair(smem_u32(&tfull[acc]));
-        umma_commit_pair(cluster_addr(&tfull[acc], 1));
+        if (!(ti == 0 && (p.test_flags & B200K_GEMM_TEST_WITHHOLD_READY))) {
+          umma_commit_pair(smem_u32(&tfull[acc]));
+          umma_commit_pair(cluster_addr(&tfull[acc], 1));
+        }
         stamp_tile(p, ti, 3);
         if (++acc == 2) {
           acc = 0;

@@ -256,6 +256,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.out_sm = a->out_stride_m;
   p.status = a->status;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 2000000000ll;
+  p.test_flags = a->test_flags;
   const uint32_t fmt = a->ab_dtype == B200K_BF16 ? 1u : 0u;
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
             (static_cast<uint32_t>(bm >> 4) << 24);
