@@ -87,6 +87,14 @@ struct Params {
   int32_t xm_bias, xm_scale, xm_res;               // how the fast path stages each operand (XM_*)
   int32_t row_idx;                                 // extras index of the fast path's full-matrix operand
   int32_t test_flags;                              // B200K_GEMM_TEST_* hooks (0 in production)
+  // Fast path: the bias (ex[f_bias]) and the full-matrix operand (ex[row_idx])
+  // copied out of `ex`, so the epilogue's hot loop reads fixed parameter slots.
+  const void* bias_ptr;
+  int64_t bias_sn;
+  int32_t bias_dt;
+  int32_t bias_vec;  // 1: unit stride, 16-byte aligned -- whole 32-column runs load as vectors
+  const void* row_ptr;
+  int64_t row_sm;
   unsigned long long* trace;                       // diagnostic timeline, null = off
   EpiOperand ex[B200K_MAX_INPUTS - 1];
   B200kProgram prog;
@@ -477,18 +485,19 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
 // ------------------------------------------- fast path, latency-hiding loop
 // Operand staging modes, chosen on the host per operand:
 //   XM_BCAST   row-broadcast f32/bf16/f16 vector (stride_m == 0, e.g. a
-//              bias): each lane loads one column of the 32-column sub-chunk
-//              (one coalesced load per warp) and the values reach every row
-//              by __shfl_sync;
+//              bias): every lane loads the sub-chunk's 32 values with
+//              warp-uniform 16-byte loads (L1 hits after the first tile; a
+//              shuffle per value instead costs more than the whole rest of
+//              a bias-only epilogue);
 //   XM_ROW16   full 16-bit matrix with unit column stride (a residual, or the
 //              `up` operand of SwiGLU): each lane loads its own row's 32
 //              values (64 bytes) into registers;
 //   XM_GENERIC anything else -- such programs run on the interpreter kernel.
 // The compiled path takes a bias in XM_BCAST and at most one of scale and
 // residual, in XM_ROW16 (its role is the kernel's ROW parameter, below).
-// Operands are loaded one 32-column sub-chunk ahead, across tile boundaries,
-// into a second register set that becomes the current one when the
-// sub-chunk is done.  The sub-chunk body exists once in the code and
+// The full-matrix operand is loaded one 32-column sub-chunk ahead, across
+// tile boundaries, into a second register set that becomes the current one
+// when the sub-chunk is done.  The sub-chunk body exists once in the code and
 // edge-of-matrix loads are out of line, which keeps the epilogue warps' hot
 // loop small enough for the instruction cache.
 enum { XM_NONE = 0, XM_BCAST = 1, XM_ROW16 = 2, XM_GENERIC = 3 };
@@ -505,7 +514,6 @@ enum { XM_NONE = 0, XM_BCAST = 1, XM_ROW16 = 2, XM_GENERIC = 3 };
 enum { ROW_NONE = 0, ROW_SCALE = 1, ROW_RES = 2, ROW_SCALE_PK = 3, ROW_RES_PK = 4 };
 
 struct FastOps {
-  float bias_b;
   uint4 row_r[4];  // the full-matrix operand's 32 values of this lane's row
 };
 
@@ -522,14 +530,68 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
-// Lane l's column n + l of a row-broadcast operand (f32, bf16 or f16).
-__device__ __forceinline__ float load_bcast(const EpiOperand& e, int n, int lane, int N) {
-  const int col = n + lane;
-  if (col >= N) return 0.0f;
-  const int64_t off = static_cast<int64_t>(col) * e.sn;
-  if (e.dt == B200K_F32) return __ldg(reinterpret_cast<const float*>(e.ptr) + off);
-  const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(e.ptr) + off);
-  return e.dt == B200K_BF16 ? __uint_as_float(static_cast<uint32_t>(u) << 16) : __half2float(__ushort_as_half(u));
+// Adds the row-broadcast bias of columns n..n+31 to v (every lane the same
+// 32 values).  A run inside [0, N) of a unit-stride, 16-byte-aligned vector
+// loads as 4 (16-bit) or 8 (f32) 16-byte vectors whose address is the same
+// for every lane, one L1 request each; edge runs and strided vectors load
+// value by value.  Each add is rounded on its own (__fadd_rn), as the
+// decomposed graph's bias add is.  (v stays in registers: no call takes it
+// by reference.)
+__device__ __forceinline__ float bias_at(const Params& p, int col) {
+  if (col >= p.N) return 0.0f;
+  const int64_t off = static_cast<int64_t>(col) * p.bias_sn;
+  if (p.bias_dt == B200K_F32) return __ldg(reinterpret_cast<const float*>(p.bias_ptr) + off);
+  const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(p.bias_ptr) + off);
+  return p.bias_dt == B200K_BF16 ? __uint_as_float(static_cast<uint32_t>(u) << 16) : __half2float(__ushort_as_half(u));
+}
+
+__device__ __forceinline__ void add_bias32(const Params& p, int n, float (&v)[32]) {
+  if (!p.bias_vec || n + 32 > p.N) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bias_at(p, n + j));
+    return;
+  }
+  if (p.bias_dt == B200K_F32) {
+    const float4* q = reinterpret_cast<const float4*>(p.bias_ptr) + (n >> 2);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b = __ldg(q + i);
+      v[4 * i] = __fadd_rn(v[4 * i], b.x);
+      v[4 * i + 1] = __fadd_rn(v[4 * i + 1], b.y);
+      v[4 * i + 2] = __fadd_rn(v[4 * i + 2], b.z);
+      v[4 * i + 3] = __fadd_rn(v[4 * i + 3], b.w);
+    }
+    return;
+  }
+  const uint4* q = reinterpret_cast<const uint4*>(p.bias_ptr) + (n >> 3);
+  uint4 w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = __ldg(q + i);
+  float b[32];
+  if (p.bias_dt == B200K_BF16) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        b[8 * i + 2 * j] = __uint_as_float(u[j] << 16);
+        b[8 * i + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
+        b[8 * i + 2 * j] = f.x;
+        b[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], b[j]);
 }
 
 // Eight 16-bit values of one row from column n, zero at and beyond column N.
@@ -544,8 +606,8 @@ static __device__ __noinline__ uint4 load_row16_edge8(const uint16_t* row, int n
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-__device__ __forceinline__ void load_row16(const EpiOperand& e, int m, int n, int M, int N, uint4 (&b)[4]) {
-  const uint16_t* row = reinterpret_cast<const uint16_t*>(e.ptr) + static_cast<int64_t>(m) * e.sm;
+__device__ __forceinline__ void load_row16(const void* ptr, int64_t sm, int m, int n, int M, int N, uint4 (&b)[4]) {
+  const uint16_t* row = reinterpret_cast<const uint16_t*>(ptr) + static_cast<int64_t>(m) * sm;
   if (m < M && n + 32 <= N) {
     const uint4* q = reinterpret_cast<const uint4*>(row + n);
 #pragma unroll
@@ -570,17 +632,15 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 template <int CW, int ROW>
 __device__ __forceinline__ void prefetch_row16_l2(const Params& p, int m, int n) {
   if (ROW == ROW_NONE || m >= p.M || n >= p.N) return;
-  const EpiOperand& e = p.ex[p.row_idx];
   const int bytes = min(CW, p.N - n) * 2;
-  const char* row = reinterpret_cast<const char*>(e.ptr) + (static_cast<int64_t>(m) * e.sm + n) * 2;
+  const char* row = reinterpret_cast<const char*>(p.row_ptr) + (static_cast<int64_t>(m) * p.row_sm + n) * 2;
   for (int off = 0; off < bytes; off += 128) prefetch_l2(row + off);
   prefetch_l2(row + bytes - 1);  // the line of the last byte when the row is not 128-byte aligned
 }
 
 template <int ROW>
-__device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, int lane, FastOps& f) {
-  if (p.f_bias >= 0) f.bias_b = load_bcast(p.ex[p.f_bias], n, lane, p.N);
-  if constexpr (ROW != ROW_NONE) load_row16(p.ex[p.row_idx], m, n, p.M, p.N, f.row_r);
+__device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, FastOps& f) {
+  if constexpr (ROW != ROW_NONE) load_row16(p.row_ptr, p.row_sm, m, n, p.M, p.N, f.row_r);
 }
 
 __device__ __forceinline__ uint32_t pk_op(uint32_t a, uint32_t b, bool bf16, bool mul) {
@@ -615,75 +675,94 @@ __device__ __forceinline__ void unpack16x8(uint4 u, int dt, float (&x)[8]) {
 
 // One 32-column sub-chunk of one output row per lane (columns n..n+31 of
 // row m, TMEM columns t_col..t_col+31): read the accumulator, apply the
-// canonical epilogue with the operands in `use`, stage, and store every
-// 128-byte staging row with one TMA store per warp.
+// canonical epilogue with the full-matrix operand in `use`, stage, and store
+// every 128-byte staging row with one TMA store per warp.  Each step runs
+// over all 32 values before the next (bias, activation, rounding, operand,
+// packing), so independent values interleave; the dtype choices are
+// warp-uniform branches around whole steps.
 template <int BN, int OUT_BYTES, int ACT, int ROW>
 __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, uint32_t t_col, int row0,
-                                               int n, int s, int lane, uint8_t* sb, const FastOps& use,
-                                               bool stamp_subs) {
+                                               int n, int s, int lane, uint8_t* sb, const FastOps& use) {
   constexpr int kEC = 128 / OUT_BYTES;
   constexpr int NSUB = Epi<BN>::CW / 32;
   constexpr int SUB_PER_STG = kEC / 32;
   constexpr bool kPacked = ROW == ROW_SCALE_PK || ROW == ROW_RES_PK;
   constexpr bool kMul = ROW == ROW_SCALE || ROW == ROW_SCALE_PK;
   static_assert(OUT_BYTES == 2 || ROW == ROW_NONE, "full-matrix operands are 16-bit, as is the output");
-  uint32_t raw[32];
-  tmem_ld32(t_col, raw);
-  tmem_wait_ld();
-  if (stamp_subs && s < 4) stamp(p, 248 + 2 * s);
+  float v[32];
+  {
+    uint32_t raw[32];
+    tmem_ld32(t_col, raw);
+    tmem_wait_ld();
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+  }
   const int sub = s % SUB_PER_STG;
   if (sub == 0) {
     if (lane == 0) bulk_wait_read_all();
     __syncwarp();
   }
-  if (stamp_subs && s < 4) stamp(p, 249 + 2 * s);
+  if (p.f_bias >= 0) add_bias32(p, n, v);
+#pragma unroll
+  for (int g = 0; g < 4; ++g) apply_act8<ACT>(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
   const bool out_bf16 = p.out_dt == B200K_BF16;
+  uint4 u[4];
+  if constexpr (kPacked) {
+    if (out_bf16) {
 #pragma unroll
-  for (int g = 0; g < 4; ++g) {
-    float v[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[g * 8 + j]);
-    if (p.f_bias >= 0) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = __fadd_rn(v[j], __shfl_sync(0xffffffffu, use.bias_b, g * 8 + j));
-    }
-    apply_act8<ACT>(v);
-    if constexpr (kPacked) {
-      uint4 u = out_bf16 ? pack_bf16x8(v) : pack_f16x8(v);
-      const uint4 r = use.row_r[g];
-      u.x = pk_op(u.x, r.x, out_bf16, kMul);
-      u.y = pk_op(u.y, r.y, out_bf16, kMul);
-      u.z = pk_op(u.z, r.z, out_bf16, kMul);
-      u.w = pk_op(u.w, r.w, out_bf16, kMul);
-      const int chunk = sub * 4 + g;
-      *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u;
-    } else {
-      if (p.f_round == B200K_BF16) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = round_bf16(v[j]);
-      } else if (p.f_round == B200K_F16) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = round_f16(v[j]);
+      for (int g = 0; g < 4; ++g) {
+        u[g] = pack_bf16x8(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
+        const uint4 r = use.row_r[g];
+        u[g] = make_uint4(pk_op(u[g].x, r.x, true, kMul), pk_op(u[g].y, r.y, true, kMul),
+                          pk_op(u[g].z, r.z, true, kMul), pk_op(u[g].w, r.w, true, kMul));
       }
-      if constexpr (ROW != ROW_NONE) {
+    } else {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        u[g] = pack_f16x8(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
+        const uint4 r = use.row_r[g];
+        u[g] = make_uint4(pk_op(u[g].x, r.x, false, kMul), pk_op(u[g].y, r.y, false, kMul),
+                          pk_op(u[g].z, r.z, false, kMul), pk_op(u[g].w, r.w, false, kMul));
+      }
+    }
+  } else {
+    if (p.f_round == B200K_BF16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = round_bf16(v[j]);
+    } else if (p.f_round == B200K_F16) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = round_f16(v[j]);
+    }
+    if constexpr (ROW != ROW_NONE) {
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
         float x[8];
         unpack16x8(use.row_r[g], out_bf16 ? B200K_BF16 : B200K_F16, x);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = kMul ? __fmul_rn(v[j], x[j]) : __fadd_rn(v[j], x[j]);
-      }
-      if constexpr (OUT_BYTES == 2) {
-        const uint4 u = out_bf16 ? pack_bf16x8(v) : pack_f16x8(v);
-        const int chunk = sub * 4 + g;
-        *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u;
-      } else {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int chunk = 2 * g + h;
-          *reinterpret_cast<float4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) =
-              make_float4(v[4 * h], v[4 * h + 1], v[4 * h + 2], v[4 * h + 3]);
-        }
+        for (int j = 0; j < 8; ++j) v[8 * g + j] = kMul ? __fmul_rn(v[8 * g + j], x[j]) : __fadd_rn(v[8 * g + j], x[j]);
       }
     }
+    if constexpr (OUT_BYTES == 2) {
+      if (out_bf16) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) u[g] = pack_bf16x8(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
+      } else {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) u[g] = pack_f16x8(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
+      }
+    }
+  }
+  if constexpr (OUT_BYTES == 2) {
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const int chunk = sub * 4 + g;
+      *reinterpret_cast<uint4*>(sb + lane * 128 + ((chunk ^ (lane & 7)) << 4)) = u[g];
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<float4*>(sb + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
   }
   if (sub == SUB_PER_STG - 1 || s + 1 == NSUB || n + 32 >= p.N) {
     fence_async_smem();
@@ -713,7 +792,7 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
     int tm, tn;
     tile_coords(t0, p, tm, tn);
     prefetch_row16_l2<CW, ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW);
-    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW, lane, cur);
+    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
@@ -742,11 +821,13 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
 #pragma unroll 1
     for (int s = 0; s < NSUB; ++s) {
       const int n = n0 + s * 32;
-      if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, lane, nxt);
-      else if (more) fast_prefetch<ROW>(p, m2, n2, lane, nxt);
+      if (stamper && ti == 0 && s < 4) stamp(p, 248 + 2 * s);
+      if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, nxt);
+      else if (more) fast_prefetch<ROW>(p, m2, n2, nxt);
       if (n < p.N)  // warp-uniform
-        fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur, stamper && ti == 0);
-      cur = nxt;
+        fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur);
+      if (stamper && ti == 0 && s < 4) stamp(p, 249 + 2 * s);
+      if constexpr (ROW != ROW_NONE) cur = nxt;
     }
     if (stamper) stamp_tile(p, ti, 5);
     tc_fence_before();

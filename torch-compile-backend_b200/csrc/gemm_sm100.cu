@@ -280,6 +280,13 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.f_scale = a->form.scale;
   p.f_res = a->form.residual;
   p.xm_bias = bias_mode;
+  if (a->form.bias >= 0) {
+    const B200kEpiOperand& e = a->extras[a->form.bias];
+    p.bias_ptr = e.ptr;
+    p.bias_sn = e.stride_n;
+    p.bias_dt = e.dtype;
+    p.bias_vec = e.stride_n == 1 && aligned16(e.ptr) ? 1 : 0;
+  }
   p.xm_scale = mode_of(a->form.scale, true);
   p.xm_res = mode_of(a->form.residual, true);
   p.trace = nullptr;
@@ -310,6 +317,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
       const bool res = a->form.residual >= 0;
       row = res ? (packed ? ROW_RES_PK : ROW_RES) : (packed ? ROW_SCALE_PK : ROW_SCALE);
       p.row_idx = role_idx;
+      p.row_ptr = a->extras[role_idx].ptr;
+      p.row_sm = a->extras[role_idx].stride_m;
     } else if (a->form.round == a->out_dtype) {
       p.f_round = -1;  // the store's own rounding is the same one
     }
