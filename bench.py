@@ -66,12 +66,18 @@ def load_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def _dominant_kernel_name() -> str:
-    """The kernel the library picks for the sweep's dominant launch."""
+# Kernel and ncu summary (profiles/<name>.md) per tile config of the dominant launch.
+_DOMINANT_KERNELS = {3: ("gemm_pair_kernel 256x256", "gemm_pair_16384x4096x14336_gelu"),
+                     4: ("gemm_pair_kernel 256x512", "gemm_pair_wide_16384x4096x14336_gelu")}
+
+
+def _dominant_kernel() -> tuple[str, str | None]:
+    """The kernel the library picks for the sweep's dominant launch and the
+    name of its ncu summary under profiles/ (None when there is none)."""
     from compiler.runtime import cabi
 
     cfg = cabi.library().b200k_gemm_pick_config(*DOMINANT)
-    return "gemm_pair_kernel" if cfg == 3 else "gemm_epilogue_kernel"
+    return _DOMINANT_KERNELS.get(cfg, ("gemm_epilogue_kernel", None))
 
 
 def profile_traffic(name: str):
@@ -359,8 +365,8 @@ def run_sweep(args, dist: Dist) -> dict:
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 3), "peak_source": f"{src} bf16_tflops_sustained",
                      "frac_of_burst": round(achieved / peaks["bf16_tflops"], 3),
-                     "kernel": _dominant_kernel_name() + " 16384x4096x14336 gelu",
-                     "traffic": profile_traffic("gemm_pair_16384x4096x14336_gelu")},
+                     "kernel": _dominant_kernel()[0] + " 16384x4096x14336 gelu",
+                     "traffic": profile_traffic(_dominant_kernel()[1]) if _dominant_kernel()[1] else None},
         "e2e": {"value": round(n * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
         "gpu_launches": args.steps * len(probs),

@@ -252,9 +252,10 @@ int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream);
 
 /* Number of GEMM tile configurations in the built-in table and their shapes
  * (block_m x block_n).  Config 2 (128 x 192 tiles) runs compiled epilogues
- * only; config 3 (256 x 256 tiles, each computed by a cluster of two CTAs on
- * two SMs) runs compiled epilogues with K-major B and 16-bit output only.  A
- * call forcing either outside its domain runs config 0 instead. */
+ * only; configs 3 and 4 (256 x 256 and 256 x 512 tiles, each computed by a
+ * cluster of two CTAs on two SMs) run compiled epilogues with K-major B and
+ * 16-bit output only.  A call forcing one outside its domain runs config 0
+ * instead. */
 int b200k_gemm_num_configs(void);
 int b200k_gemm_config_info(int config, int* block_m, int* block_n, int* block_k, int* stages);
 /* The configuration b200k_gemm_epilogue picks for a problem with a compiled

@@ -37,7 +37,7 @@ def test_library_answers_without_gpu():
     assert n >= 2
     bm, bn, bk, st = (ctypes.c_int(), ctypes.c_int(), ctypes.c_int(), ctypes.c_int())
     assert lib.b200k_gemm_config_info(0, ctypes.byref(bm), ctypes.byref(bn), ctypes.byref(bk), ctypes.byref(st)) == 0
-    assert bm.value in (128, 256) and bk.value == 64 and bn.value in (128, 192, 256)
+    assert bm.value in (128, 256) and bk.value == 64 and bn.value in (128, 192, 256, 512)
     assert lib.b200k_gemm_config_info(n, None, None, None, None) == 1  # B200K_ERR_ARG
 
 

@@ -145,7 +145,7 @@ def test_gemm_sweep_configs(shape, act, path):
 
 @pytest.mark.parametrize("M,N,K", [(1, 8, 8), (37, 72, 24), (128, 256, 64), (130, 260, 72), (300, 100, 136),
                                    (257, 1000, 768), (64, 4096, 1024)])
-@pytest.mark.parametrize("config", [0, 1, 2, 3])
+@pytest.mark.parametrize("config", [0, 1, 2, 3, 4])
 @pytest.mark.parametrize("ab", ["bfloat16", "float16"])
 @pytest.mark.parametrize("path", ["compiled", "interpreted"])
 def test_gemm_edge_shapes(M, N, K, config, ab, path):
@@ -171,13 +171,17 @@ def test_gemm_edge_shapes(M, N, K, config, ab, path):
     _assert_close(out, want, *_gemm_tol(want))
 
 
+@pytest.mark.parametrize("pair_cfg", [3, 4])
 @pytest.mark.parametrize("act", ["none", "gelu", "silu"])
-@pytest.mark.parametrize("shape", [(256, 256, 64), (4096, 4096, 4096), (2000, 3000, 1600), (300, 520, 2048)])
-def test_gemm_pair_tiles_equal_single_cta_tiles(act, shape):
-    """256 x 256 tiles on CTA pairs (config 3, tcgen05 cta_group::2) against
-    128 x 256 tiles on single CTAs (config 0): the same MMAs over the same K
-    order and the same epilogue, so the outputs are equal bit for bit, full
-    and ragged tiles alike; and the fp32 oracle agrees on sampled rows."""
+@pytest.mark.parametrize("shape", [(256, 256, 64), (4096, 4096, 4096), (2000, 3000, 1600), (300, 520, 2048),
+                                   (12608, 768, 3072), (1000, 1300, 4160)])
+def test_gemm_pair_tiles_equal_single_cta_tiles(pair_cfg, act, shape):
+    """256 x 256 and 256 x 512 tiles on CTA pairs (configs 3 and 4, tcgen05
+    cta_group::2) against 128 x 256 tiles on single CTAs (config 0): the same
+    MMAs over the same K order and the same epilogue, so the outputs are
+    equal bit for bit, full and ragged tiles alike (N = 1300: a 512-wide tile
+    whose second half is partly and wholly past N); and the fp32 oracle
+    agrees on sampled rows."""
     M, N, K = shape
     g = torch.Generator(device=DEV).manual_seed(M + N + K)
     x = (0.02 * torch.randn(M, K, device=DEV, generator=g)).to(torch.bfloat16)
@@ -186,7 +190,7 @@ def test_gemm_pair_tiles_equal_single_cta_tiles(act, shape):
     r = (0.02 * torch.randn(M, N, device=DEV, generator=g)).to(torch.bfloat16)
     code, imm, spec, form = epilogue_program(act, residual=True)
     outs = []
-    for cfg in (3, 0):
+    for cfg in (pair_cfg, 0):
         out = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
         status = torch.zeros(1, dtype=torch.int32, device=DEV)
         cabi.gemm_epilogue(x, w.t(), [b, r], code, imm, out, tile_config=cfg, status=status, form=form)
@@ -237,7 +241,7 @@ def role_program(act: str, role: str, round_to: str | None):
 @pytest.mark.parametrize("act", ["none", "silu", "gelu"])
 @pytest.mark.parametrize("dt", ["bfloat16", "float16"])
 @pytest.mark.parametrize("rounded", [True, False])
-@pytest.mark.parametrize("config", [0, 1, 2, 3])
+@pytest.mark.parametrize("config", [0, 1, 2, 3, 4])
 def test_gemm_row_operand_roles(role, act, dt, rounded, config):
     """A full 16-bit matrix as residual or scale, after an activation that is
     (rounded) or is not rounded to the output type first.  Rounded, the
@@ -513,7 +517,7 @@ def test_rope_matches_eager_bit_for_bit(dtype, case):
 
 
 # ------------------------------------------------------------- failure detection
-@pytest.mark.parametrize("config", [0, 3])
+@pytest.mark.parametrize("config", [0, 3, 4])
 def test_gemm_stalled_wait_times_out_and_context_survives(config):
     """A wait that nothing completes (the test hook withholds the first
     tile's accumulator-ready signal) runs out after the 50 ms limit: the

@@ -37,9 +37,10 @@ CU_UNITS = [(src, os.path.splitext(src)[0], []) for src in ("capi.cu", "pointwis
                                                                   "rope.cu", "gemm_sm100.cu")]
 CU_UNITS += [("gemm_fast.cu", f"gemm_fast_{bn}_{act}", [f"-DB200K_FAST_BN={bn}", f"-DB200K_FAST_ACT={act}"])
              for bn in (256, 192, 128) for act in (0, 1, 2, 3, 4)]
-# ... and once per activation for the CTA-pair (256 x 256 tile) kernels
-CU_UNITS += [("gemm_fast.cu", f"gemm_fast_pair_{act}", ["-DB200K_FAST_BN=2", f"-DB200K_FAST_ACT={act}"])
-             for act in (0, 1, 2, 3, 4)]
+# ... and once per activation for the CTA-pair kernels (2: 256 x 256 tiles,
+# 4: 256 x 512 tiles)
+CU_UNITS += [("gemm_fast.cu", f"gemm_fast_pair{w}_{act}", [f"-DB200K_FAST_BN={w}", f"-DB200K_FAST_ACT={act}"])
+             for w in (2, 4) for act in (0, 1, 2, 3, 4)]
 HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h", "gemm_kernel.cuh", "rowreduce.cuh")] + [
     os.path.join(INCLUDE, "b200k.h")]
 LIB = os.path.join(OUT_DIR, "libb200k.so")

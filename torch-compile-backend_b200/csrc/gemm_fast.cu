@@ -7,25 +7,36 @@
 #include "gemm_kernel.cuh"
 
 #if !defined(B200K_FAST_BN) || !defined(B200K_FAST_ACT)
-#error "compile with -DB200K_FAST_BN=<256|192|128|2> -DB200K_FAST_ACT=<activation> (2: the CTA-pair kernels)"
+#error "compile with -DB200K_FAST_BN=<256|192|128|2|4> -DB200K_FAST_ACT=<activation> (2, 4: the CTA-pair kernels)"
 #endif
 
 namespace b200k {
 namespace gemm {
 
-#if B200K_FAST_BN == 2
-// CTA-pair kernels: 256 x 256 tiles on two-CTA clusters, 16-bit output.
+#if B200K_FAST_BN == 2 || B200K_FAST_BN == 4
+// CTA-pair kernels, 16-bit output: B200K_FAST_BN 2 builds the 256 x 256 tiles
+// (config 3, launch_pair_<ACT>), 4 the 256 x 512 tiles (config 4,
+// launch_pairw_<ACT>).
+constexpr bool kWide = B200K_FAST_BN == 4;
+constexpr int kPairCfg = kWide ? 4 : 3;
+static_assert(kConfigs[kPairCfg].bm == 2 * BM && kConfigs[kPairCfg].bn == (kWide ? 2 : 1) * kPairMmaN,
+              "pair tile configs");
+constexpr int kStages = kConfigs[kPairCfg].stages;
+#if B200K_FAST_BN == 4
+#define B200K_PAIR_FN2(ACT) launch_pairw_##ACT
+#else
 #define B200K_PAIR_FN2(ACT) launch_pair_##ACT
+#endif
 #define B200K_PAIR_FN(ACT) B200K_PAIR_FN2(ACT)
 int B200K_PAIR_FN(B200K_FAST_ACT)(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                                   const Params& p, int grid, cudaStream_t st) {
   constexpr int kAct = B200K_FAST_ACT;
   switch (row) {
-    case ROW_NONE: return launch_pair<kPairStages, 2, kAct, ROW_NONE>(ta, tb, to, p, grid, st);
-    case ROW_SCALE: return launch_pair<kPairStages, 2, kAct, ROW_SCALE>(ta, tb, to, p, grid, st);
-    case ROW_RES: return launch_pair<kPairStages, 2, kAct, ROW_RES>(ta, tb, to, p, grid, st);
-    case ROW_SCALE_PK: return launch_pair<kPairStages, 2, kAct, ROW_SCALE_PK>(ta, tb, to, p, grid, st);
-    case ROW_RES_PK: return launch_pair<kPairStages, 2, kAct, ROW_RES_PK>(ta, tb, to, p, grid, st);
+    case ROW_NONE: return launch_pair<kStages, 2, kAct, ROW_NONE, kWide>(ta, tb, to, p, grid, st);
+    case ROW_SCALE: return launch_pair<kStages, 2, kAct, ROW_SCALE, kWide>(ta, tb, to, p, grid, st);
+    case ROW_RES: return launch_pair<kStages, 2, kAct, ROW_RES, kWide>(ta, tb, to, p, grid, st);
+    case ROW_SCALE_PK: return launch_pair<kStages, 2, kAct, ROW_SCALE_PK, kWide>(ta, tb, to, p, grid, st);
+    case ROW_RES_PK: return launch_pair<kStages, 2, kAct, ROW_RES_PK, kWide>(ta, tb, to, p, grid, st);
     default: return B200K_ERR_UNSUPPORTED;
   }
 }

@@ -51,7 +51,14 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;  // one 128-byte swizzle atom of 16-bit elements
 constexpr int UMMA_K = 16;
+// Tile rows per raster group (Params::group_m): a wave of persistent CTAs
+// walks group_m tile rows down before moving right, so the A rows and B
+// columns it reads at once stay in L2.  The per-wave working set
+// group_m * (A bytes of a tile row) + (slots / group_m) * (B bytes of a tile
+// column) is smallest near group_m = sqrt(slots * B / A): 16 for 128 x 256
+// tiles on 148 SMs, 8 for the 74 CTA pairs of 256-row tiles.
 constexpr int kGroupM = 16;
+constexpr int kGroupMPair = 8;
 
 // Epilogue warp layout of a BN-wide tile: NG column groups of CW columns,
 // one warp per (TMEM lane quarter, column group); warps 0-3 are control.
@@ -87,6 +94,7 @@ struct Params {
   int32_t xm_bias, xm_scale, xm_res;               // how the fast path stages each operand (XM_*)
   int32_t row_idx;                                 // extras index of the fast path's full-matrix operand
   int32_t test_flags;                              // B200K_GEMM_TEST_* hooks (0 in production)
+  int32_t group_m;                                 // tile rows per raster group (tile_coords)
   // Fast path: the bias (ex[f_bias]) and the full-matrix operand (ex[row_idx])
   // copied out of `ex`, so the epilogue's hot loop reads fixed parameter slots.
   const void* bias_ptr;
@@ -285,10 +293,10 @@ __device__ __forceinline__ void stamp_tile(const Params& p, int i, int field) {
 }
 
 __device__ __forceinline__ void tile_coords(int t, const Params& p, int& tm, int& tn) {
-  const int per_group = kGroupM * p.tiles_n;
+  const int per_group = p.group_m * p.tiles_n;
   const int g = t / per_group;
-  const int first_m = g * kGroupM;
-  const int gsize = min(p.tiles_m - first_m, kGroupM);
+  const int first_m = g * p.group_m;
+  const int gsize = min(p.tiles_m - first_m, p.group_m);
   const int r = t - g * per_group;
   tm = first_m + r % gsize;
   tn = r / gsize;
@@ -774,16 +782,23 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
   }
 }
 
-// PAIR: the tiles are 256 x BN, one per CTA pair (the grid's cluster index
-// walks them), and this CTA's 128 rows start at `rank` x 128; the
-// accumulator is released on the even CTA's barrier (`tempty_even`).
-template <int BN, int OUT_BYTES, int ACT, int ROW, bool PAIR = false>
+// PAIR: the tiles are 256 rows high, one per CTA pair (the grid's cluster
+// index walks them), and this CTA's 128 rows start at `rank` x 128; the
+// accumulator is released on the even CTA's barrier.
+// WIDE (pairs only): the tile is 256 x 2*BN and its accumulator is the whole
+// 512-column TMEM allocation in two BN-column halves.  tfull[0] signals the
+// tile; half h is released on tempty[h] as soon as it has been read, so the
+// next tile's MMAs into half 0 start while half 1 is still being drained.
+template <int BN, int OUT_BYTES, int ACT, int ROW, bool PAIR = false, bool WIDE = false>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
                                                    uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
                                                    int cg, int lane, const Ctl& ctl, uint32_t rank = 0) {
+  static_assert(PAIR || !WIDE, "wide tiles run on CTA pairs");
   constexpr int CW = Epi<BN>::CW;
-  constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and tile
+  constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and accumulator half
   constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile
+  constexpr int H = WIDE ? 2 : 1;         // accumulator halves per tile
+  constexpr int TN = H * BN;              // columns per tile
   const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
   const int step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
   const int rank_rows = static_cast<int>(rank) * BM;
@@ -791,8 +806,10 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
   if (t0 < p.num_tiles) {
     int tm, tn;
     tile_coords(t0, p, tm, tn);
-    prefetch_row16_l2<CW, ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW);
-    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * BN + cg * CW, cur);
+#pragma unroll
+    for (int h = 0; h < H; ++h)
+      prefetch_row16_l2<CW, ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + h * BN + cg * CW);
+    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + cg * CW, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
@@ -807,36 +824,44 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       int tm2, tn2;
       tile_coords(t + step, p, tm2, tn2);
       m2 = tm2 * TM + rank_rows + quarter * 32 + lane;
-      n2 = tn2 * BN + cg * CW;
-      prefetch_row16_l2<CW, ROW>(p, m2, n2);
+      n2 = tn2 * TN + cg * CW;
+#pragma unroll
+      for (int h = 0; h < H; ++h) prefetch_row16_l2<CW, ROW>(p, m2, n2 + h * BN);
     }
     if (!wait_bar(&tfull[acc], aph, ctl)) break;
     tc_fence_after();
     if (stamper) stamp_tile(p, ti, 4);
     const int row0 = tm * TM + rank_rows + quarter * 32;
     const int m = row0 + lane;
-    const int n0 = tn * BN + cg * CW;
-    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                           static_cast<uint32_t>(acc * BN + cg * CW);
 #pragma unroll 1
-    for (int s = 0; s < NSUB; ++s) {
-      const int n = n0 + s * 32;
-      if (stamper && ti == 0 && s < 4) stamp(p, 248 + 2 * s);
-      if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, nxt);
-      else if (more) fast_prefetch<ROW>(p, m2, n2, nxt);
-      if (n < p.N)  // warp-uniform
-        fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur);
-      if (stamper && ti == 0 && s < 4) stamp(p, 249 + 2 * s);
-      if constexpr (ROW != ROW_NONE) cur = nxt;
+    for (int h = 0; h < H; ++h) {
+      const int n0 = tn * TN + h * BN + cg * CW;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>((WIDE ? h : acc) * BN + cg * CW);
+#pragma unroll 1
+      for (int s = 0; s < NSUB; ++s) {
+        const int n = n0 + s * 32;
+        if (stamper && ti == 0 && h == 0 && s < 4) stamp(p, 248 + 2 * s);
+        if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, nxt);
+        else if (h + 1 < H) fast_prefetch<ROW>(p, m, n0 + BN, nxt);
+        else if (more) fast_prefetch<ROW>(p, m2, n2, nxt);
+        if (n < p.N)  // warp-uniform
+          fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur);
+        if (stamper && ti == 0 && h == 0 && s < 4) stamp(p, 249 + 2 * s);
+        if constexpr (ROW != ROW_NONE) cur = nxt;
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        uint64_t* rel = &tempty[WIDE ? h : acc];
+        if (PAIR && rank != 0) mbar_arrive_cluster(cluster_addr(rel, 0));
+        else mbar_arrive(rel);
+      }
     }
     if (stamper) stamp_tile(p, ti, 5);
-    tc_fence_before();
-    __syncwarp();
-    if (lane == 0) {
-      if (PAIR && rank != 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
-      else mbar_arrive(&tempty[acc]);
-    }
-    if (++acc == 2) {
+    if (WIDE) {
+      aph ^= 1u;
+    } else if (++acc == 2) {
       acc = 0;
       aph ^= 1u;
     }
@@ -1076,33 +1101,47 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
 }
 
 // ------------------------------------------------------------ CTA-pair kernel
-// 256 x 256 tiles on a cluster of two CTAs (compiled epilogues, K-major B).
-// Per CTA: a STAGES-deep ring of its own 128 A rows and its half (128 rows)
-// of the tile's B rows (32 KB a stage instead of 48 KB for one CTA's 128 x
-// 256 tile: the pair shares B), two 256-column accumulators allocated as a
-// pair, and eight epilogue warps on its own 128 rows.  Barriers: full[s] and
-// tempty[a] live in the even CTA (the odd CTA's loads and epilogue complete
-// and arrive there); empty[s] and tfull[a] in both CTAs (the even CTA's MMA
-// thread commits to each copy).  Every wait is bounded as in the one-CTA
-// kernel; cluster barriers open and close the kernel so that no CTA leaves
-// while the other may still signal one of its barriers.
-constexpr int kPairBN = 256;
-template <int STAGES, int OUT_BYTES>
+// 256-row tiles on a cluster of two CTAs (compiled epilogues, K-major B),
+// the MMAs tcgen05 cta_group::2 with M = 256 and N = 256, each CTA supplying
+// its own 128 A rows and half (128 rows) of each MMA's B rows.
+//   narrow (WIDE = false): 256 x 256 tiles, a 32 KB stage per CTA (its A rows
+//     and B half: a third less operand traffic per FLOP than one CTA's
+//     128 x 256 tile), two 256-column accumulators, so a tile's epilogue
+//     overlaps the next tile's MMAs;
+//   wide (WIDE = true): 256 x 512 tiles, two MMAs per K step, one into each
+//     256-column half of a single 512-column accumulator; a 48 KB stage per
+//     CTA (its A rows and a B half for each MMA) carries 4/3 the FLOPs per
+//     byte of the narrow tile.  The B200 tensor pipe outruns the operand
+//     loads of the narrow tile (measured ~2030 TFLOP/s with the loads
+//     removed, ~1450-1500 with them), so the wider tile's lower traffic per
+//     FLOP is the one that pays; the price is that the next tile's MMAs
+//     wait for the epilogue to release each half.
+// Barriers: full[s] and tempty[a] live in the even CTA (the odd CTA's loads
+// and epilogue complete and arrive there); empty[s] and tfull[a] in both
+// CTAs (the even CTA's MMA thread commits to each copy).  Every wait is
+// bounded as in the one-CTA kernel; cluster barriers open and close the
+// kernel so that no CTA leaves while the other may still signal one of its
+// barriers.
+constexpr int kPairMmaN = 256;
+template <int STAGES, int OUT_BYTES, bool WIDE>
 struct PairCfg {
+  static constexpr int kHalves = WIDE ? 2 : 1;  // MMAs (and B halves) per K step
   static constexpr uint32_t kABytes = BM * BK * 2;
-  static constexpr uint32_t kBBytes = (kPairBN / 2) * BK * 2;
+  static constexpr uint32_t kBHalfBytes = (kPairMmaN / 2) * BK * 2;
+  static constexpr uint32_t kBBytes = kHalves * kBHalfBytes;
   static constexpr uint32_t kTmemCols = 512;
-  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<kPairBN>::kWarps * kStgBytes;
+  static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<kPairMmaN>::kWarps * kStgBytes;
   static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
 };
 
-template <int STAGES, int OUT_BYTES, int ACT, int ROW>
-__global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
+template <int STAGES, int OUT_BYTES, int ACT, int ROW, bool WIDE>
+__global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
-  using C = PairCfg<STAGES, OUT_BYTES>;
+  using C = PairCfg<STAGES, OUT_BYTES, WIDE>;
+  constexpr int TN = C::kHalves * kPairMmaN;  // tile columns
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* sbase = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
@@ -1130,7 +1169,7 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 2 * Epi<kPairBN>::kWarps);
+      mbar_init(&tempty[a], 2 * Epi<kPairMmaN>::kWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -1176,8 +1215,10 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
           const uint32_t fb = cluster_addr(&full[s], 0);
           if (even) mbar_arrive_expect_tx(&full[s], kTx);
           tma_load_2d_pair(sA + s * C::kABytes, &tmA, fb, kb * BK, tm * (2 * BM) + static_cast<int>(rank) * BM);
-          tma_load_2d_pair(sB + s * C::kBBytes, &tmB, fb, kb * BK,
-                           tn * kPairBN + static_cast<int>(rank) * (kPairBN / 2));
+#pragma unroll
+          for (int h = 0; h < C::kHalves; ++h)
+            tma_load_2d_pair(sB + s * C::kBBytes + h * C::kBHalfBytes, &tmB, fb, kb * BK,
+                             tn * TN + h * kPairMmaN + static_cast<int>(rank) * (kPairMmaN / 2));
           ++issued;
           if (++s == STAGES) {
             s = 0;
@@ -1200,22 +1241,36 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
       bool ok = true;
       int ti = 0;
       for (int t = cid; t < p.num_tiles && ok; t += ncl, ++ti) {
-        if (!wait_bar(&tempty[acc], aph ^ 1u, ctl)) break;
-        tc_fence_after();
+        if (!WIDE) {
+          if (!wait_bar(&tempty[acc], aph ^ 1u, ctl)) break;
+          tc_fence_after();
+        }
         stamp_tile(p, ti, 2);
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kPairBN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = 0; kb < p.k_blocks && ok; ++kb) {
           if (!wait_bar(&full[s], ph, ctl)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t a0 = smem_u32(sA + s * C::kABytes);
-          const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
 #pragma unroll
-          for (int k = 0; k < BK / UMMA_K; ++k)
-            umma_f16_pair(d_tmem, sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024),
-                          sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024), p.idesc, (kb | k) != 0 ? 1u : 0u);
+          for (int h = 0; h < C::kHalves; ++h) {
+            if (WIDE && kb == 0) {
+              // the previous tile's epilogue has read this half
+              if (!wait_bar(&tempty[h], (static_cast<uint32_t>(ti) & 1u) ^ 1u, ctl)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((WIDE ? h : acc) * kPairMmaN);
+            const uint32_t b0 = smem_u32(sB + s * C::kBBytes + h * C::kBHalfBytes);
+#pragma unroll
+            for (int k = 0; k < BK / UMMA_K; ++k)
+              umma_f16_pair(d_tmem, sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024),
+                            sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024), p.idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          if (!ok) break;
           umma_commit_pair(smem_u32(&empty[s]));
           umma_commit_pair(cluster_addr(&empty[s], 1));
           if (++s == STAGES) {
@@ -1229,7 +1284,7 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
           umma_commit_pair(cluster_addr(&tfull[acc], 1));
         }
         stamp_tile(p, ti, 3);
-        if (++acc == 2) {
+        if (!WIDE && ++acc == 2) {
           acc = 0;
           aph ^= 1u;
         }
@@ -1242,8 +1297,9 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int ew = warp - 4;
-    epilogue_fast_loop<kPairBN, OUT_BYTES, ACT, ROW, true>(p, &tmO, tmem_base, tfull, tempty,
-                                                          sStg + ew * kStgBytes, warp & 3, ew >> 2, lane, ctl, rank);
+    epilogue_fast_loop<kPairMmaN, OUT_BYTES, ACT, ROW, true, WIDE>(p, &tmO, tmem_base, tfull, tempty,
+                                                                   sStg + ew * kStgBytes, warp & 3, ew >> 2, lane,
+                                                                   ctl, rank);
   }
 
   tc_fence_before();
@@ -1256,11 +1312,11 @@ __global__ void __launch_bounds__(Epi<kPairBN>::kThreads, 1)
   }
 }
 
-template <int STAGES, int OB, int ACT, int ROW>
+template <int STAGES, int OB, int ACT, int ROW, bool WIDE>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
                 cudaStream_t st) {
-  using C = PairCfg<STAGES, OB>;
-  auto kern = gemm_pair_kernel<STAGES, OB, ACT, ROW>;
+  using C = PairCfg<STAGES, OB, WIDE>;
+  auto kern = gemm_pair_kernel<STAGES, OB, ACT, ROW, WIDE>;
   static bool attr_set = false;  // per instantiation; idempotent
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
@@ -1270,7 +1326,7 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
   cudaLaunchConfig_t cfg;
   std::memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3(Epi<kPairBN>::kThreads, 1, 1);
+  cfg.blockDim = dim3(Epi<kPairMmaN>::kThreads, 1, 1);
   cfg.dynamicSmemBytes = C::kSmem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -1287,10 +1343,10 @@ int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap&
 struct TileConfig {
   int bm, bn, stages;  // bm 256: a CTA pair per tile
 };
-// Config 2 (192-wide tiles, twelve epilogue warps) and config 3 (256 x 256
-// tiles on CTA pairs) exist for compiled epilogues only; config 3 also needs
-// K-major B and 16-bit output.
-constexpr TileConfig kConfigs[] = {{128, 256, 4}, {128, 128, 6}, {128, 192, 4}, {256, 256, 6}};
+// Config 2 (192-wide tiles, twelve epilogue warps) and configs 3 and 4
+// (256 x 256 and 256 x 512 tiles on CTA pairs) exist for compiled epilogues
+// only; the pair configs also need K-major B and 16-bit output.
+constexpr TileConfig kConfigs[] = {{128, 256, 4}, {128, 128, 6}, {128, 192, 4}, {256, 256, 6}, {256, 512, 4}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
 template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW>
@@ -1335,17 +1391,20 @@ B200K_DECLARE_FAST(192, 2)
 B200K_DECLARE_FAST(192, 3)
 B200K_DECLARE_FAST(192, 4)
 #undef B200K_DECLARE_FAST
-// CTA-pair kernels (256 x 256 tiles, K-major B, 16-bit output, every row role).
+// CTA-pair kernels (K-major B, 16-bit output, every row role): launch_pair_*
+// runs the 256 x 256 tiles (config 3), launch_pairw_* the 256 x 512 tiles
+// (config 4).
 #define B200K_DECLARE_PAIR(ACT)                                                                                   \
   int launch_pair_##ACT(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, \
-                        int grid, cudaStream_t st);
+                        int grid, cudaStream_t st);                                                               \
+  int launch_pairw_##ACT(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,            \
+                         const Params& p, int grid, cudaStream_t st);
 B200K_DECLARE_PAIR(0)
 B200K_DECLARE_PAIR(1)
 B200K_DECLARE_PAIR(2)
 B200K_DECLARE_PAIR(3)
 B200K_DECLARE_PAIR(4)
 #undef B200K_DECLARE_PAIR
-constexpr int kPairStages = 6;
 
 }  // namespace gemm
 }  // namespace b200k

@@ -96,17 +96,22 @@ int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) 
   // from K = 2048 up (4096^3 1148 -> 1321 TFLOP/s, 16384 x 4096 x 14336 with
   // GELU 1342 -> 1502), no faster at K = 768, where the epilogue bounds a tile
   // and the 192-wide tile's twelve epilogue warps win; pairs need K >= 1536.
-  pair_ok = pair_ok && K >= 1536;
+  // The 256 x 512 pair tile moves 3/4 of the operand bytes per FLOP of the
+  // 256 x 256 one, but its single accumulator makes each tile's MMAs wait
+  // for the previous tile's epilogue (~10-20 us): measured on B200, 16384 x
+  // 4096 x 14336 with GELU 1410.6 -> 1295.0 us, 8192^3 754.0 -> 759.3 us,
+  // 4096^3 106.0 -> 122.6 us, so it is taken only from K = 12288 up.
   int best = 0;
   double best_cost = 1e300;
   for (int c = 0; c < kNumConfigs; ++c) {
     const int bm = kConfigs[c].bm, bn = kConfigs[c].bn;
     const bool pair = bm == 2 * BM;
-    if ((bn == 192 && !compiled) || (pair && !pair_ok)) continue;
+    const bool wide = pair && bn == 2 * kPairMmaN;
+    if ((bn == 192 && !compiled) || (pair && !pair_ok) || (wide && K < 12288)) continue;
     const int64_t tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const int64_t slots = pair ? sms / 2 : sms;  // tiles that run at once
     const int64_t waves = (tiles + slots - 1) / slots;
-    const double per_col = pair ? 0.9 : (bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5));
+    const double per_col = wide ? 0.82 : pair ? 0.9 : (bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5));
     const double cost = static_cast<double>(waves) * bn * per_col;
     if (cost < best_cost) {
       best_cost = cost;
@@ -116,16 +121,19 @@ int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) 
   return best;
 }
 
-int launch_pair(int act, int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+int launch_pair(bool wide, int act, int row, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                 const Params& p, int grid, cudaStream_t st) {
+#define B200K_PAIR_CASE(ACT) \
+  case ACT: return wide ? launch_pairw_##ACT(row, ta, tb, to, p, grid, st) : launch_pair_##ACT(row, ta, tb, to, p, grid, st);
   switch (act) {
-    case 0: return launch_pair_0(row, ta, tb, to, p, grid, st);
-    case 1: return launch_pair_1(row, ta, tb, to, p, grid, st);
-    case 2: return launch_pair_2(row, ta, tb, to, p, grid, st);
-    case 3: return launch_pair_3(row, ta, tb, to, p, grid, st);
-    case 4: return launch_pair_4(row, ta, tb, to, p, grid, st);
+    B200K_PAIR_CASE(0)
+    B200K_PAIR_CASE(1)
+    B200K_PAIR_CASE(2)
+    B200K_PAIR_CASE(3)
+    B200K_PAIR_CASE(4)
     default: return B200K_ERR_UNSUPPORTED;
   }
+#undef B200K_PAIR_CASE
 }
 
 }  // namespace gemm
@@ -238,6 +246,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const int bn = kConfigs[cfg].bn;
   const int bm = kConfigs[cfg].bm;
   const bool pair = bm == 2 * BM;
+  const bool wide = pair && bn == 2 * kPairMmaN;
+  const int mma_n = pair ? kPairMmaN : bn;  // N of one tcgen05.mma
 
   Params p;
   std::memset(&p, 0, sizeof(p));
@@ -258,8 +268,9 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 2000000000ll;
   p.test_flags = a->test_flags;
   const uint32_t fmt = a->ab_dtype == B200K_BF16 ? 1u : 0u;
-  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) | (static_cast<uint32_t>(bn >> 3) << 17) |
-            (static_cast<uint32_t>(bm >> 4) << 24);
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) |
+            (static_cast<uint32_t>(mma_n >> 3) << 17) | (static_cast<uint32_t>(bm >> 4) << 24);
+  p.group_m = pair ? kGroupMPair : kGroupM;
   for (int i = 0; i < a->n_extras; ++i) {
     const B200kEpiOperand& e = a->extras[i];
     EpiOperand& q = p.ex[i];
@@ -297,8 +308,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (bnm) {
     if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * 2, 64, BK)) return B200K_ERR_LAUNCH;
   } else {
-    // a CTA of a pair loads its half of the tile's B rows
-    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, pair ? bn / 2 : bn))
+    // a CTA of a pair loads its half of each MMA's B rows
+    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, pair ? kPairMmaN / 2 : bn))
       return B200K_ERR_LAUNCH;
   }
   p.direct_store = tma_out ? 0 : 1;
@@ -322,7 +333,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     } else if (a->form.round == a->out_dtype) {
       p.f_round = -1;  // the store's own rounding is the same one
     }
-    if (pair) return launch_pair(a->form.act, row, ta, tb, to, p, grid, st);
+    if (pair) return launch_pair(wide, a->form.act, row, ta, tb, to, p, grid, st);
     return launch_fast(bn, a->form.act, bnm, ob, row, ta, tb, to, p, grid, st);
   }
   if (cfg == 0) return launch_interp<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
