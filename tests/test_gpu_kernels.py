@@ -378,7 +378,8 @@ def test_pointwise_empty_is_noop():
 
 
 # ------------------------------------------------------------- row kernels
-@pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768), (9, 2048)])
+@pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768), (9, 2048),
+                                       (6, 1536), (5, 3072), (4, 6144)])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 @pytest.mark.parametrize("flags", [7, 1])
 def test_rms_norm_swiglu(rows, cols, dtype, flags):
@@ -402,7 +403,7 @@ def test_rms_norm_swiglu(rows, cols, dtype, flags):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
-@pytest.mark.parametrize("cols", [2048, 768, 100])
+@pytest.mark.parametrize("cols", [2048, 768, 100, 1536, 3072])
 def test_rms_norm(dtype, cols):
     dt = _tdt(dtype)
     x = torch.randn(67, cols, device=DEV).to(dt)
@@ -417,7 +418,7 @@ def test_rms_norm(dtype, cols):
     _assert_close(out, want, *tol)
 
 
-@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50), (5, 16384)])
+@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50), (5, 16384), (7, 1536), (9, 3072)])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 def test_layer_norm(rows, cols, dtype):
     dt = _tdt(dtype)
@@ -437,7 +438,8 @@ def test_layer_norm(rows, cols, dtype):
     _assert_close(rstd[sel], r[:, 0], 1e-4, 1e-5)
 
 
-@pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768), (6, 8192), (5, 2048)])
+@pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768), (6, 8192), (5, 2048),
+                                       (5, 768), (3, 1536), (4, 3072)])
 @pytest.mark.parametrize("log", [False, True])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 def test_softmax(rows, cols, log, dtype):

@@ -415,6 +415,36 @@ def test_patchify_lowers_patch_conv_to_gemm(bias):
     y = p @ w.view(32, 768).t() + (model.proj.bias.float() if bias else 0)
     ref = torch.nn.functional.conv2d(x, w, model.proj.bias.float() if bias else None, stride=16)
     torch.testing.assert_close(y.view(2, 4, 4, 32).permute(0, 3, 1, 2), ref, rtol=1e-4, atol=1e-4)
+    # flatten(2).transpose(1, 2): the GEMM's [B*HW, OC] rows are the tokens, so
+    # the transpose and the NCHW copy are gone and the result is a view
+    assert torch.ops.aten.transpose.int not in targets and torch.ops.aten.clone.default not in targets
+    im2col = [n for n in gm.graph.nodes if n.target == torch.ops.b200.pointwise.default]
+    assert len(im2col) == 1 and im2col[0].meta["b200_kernel"].startswith("im2col")
+    assert list(im2col[0].args[3]) == [2, 4, 4, 3, 16, 16]
+    out = [n for n in gm.graph.nodes if n.op == "output"][0].args[0][0]
+    val = out.meta["val"]
+    assert tuple(val.shape) == (2, 16, 32) and val.is_contiguous()
+
+
+def test_patchify_keeps_the_nchw_layout_for_other_uses():
+    """A patch convolution whose result is used as an image (here: a
+    pointwise op on the NCHW tensor) gets the permute-back copy, so every
+    later node sees the layout it was traced with."""
+
+    class PatchAct(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.proj = nn.Conv2d(3, 32, 16, 16)
+
+        def forward(self, img):
+            return torch.relu(self.proj(img))
+
+    (gm,) = fused_graphs(PatchAct().to(torch.bfloat16), (torch.randn(2, 3, 64, 64).to(torch.bfloat16),))
+    targets = [n.target for n in gm.graph.nodes if n.op == "call_function"]
+    assert torch.ops.aten.convolution.default not in targets
+    clones = [n for n in gm.graph.nodes if n.target == torch.ops.aten.clone.default]
+    assert len(clones) == 1 and tuple(clones[0].meta["val"].shape) == (2, 32, 4, 4)
+    assert clones[0].meta["val"].is_contiguous()
 
 
 def test_patchify_leaves_overlapping_convolutions():

@@ -363,6 +363,14 @@ __global__ void __launch_bounds__(kRowThreads, min_ctas<2 * VPT>()) swiglu16_ker
 // at most 16 vectors per thread over all segments; false past 256 threads
 // (the generic kernels take such rows).
 bool pick16(int64_t nvec, int nseg, int& tpr, int& vpt) {
+  // A warp per row that the row fills exactly (FULL: no clamped lanes): rows
+  // of 768, 1536 and 3072 16-bit values take 3, 6 and 12 vectors per lane.
+  for (int vv : {3, 4, 6, 8, 12, 16})
+    if (vv * nseg <= 16 && 32 * vv == nvec) {
+      tpr = 32;
+      vpt = vv;
+      return true;
+    }
   for (int tt : {32, 64, 128, 256})
     for (int vv : {4, 8, 16})
       if (vv * nseg <= 16 && static_cast<int64_t>(tt) * vv >= nvec) {
@@ -391,7 +399,7 @@ int launch_tv(int tpr, int vpt, bool bf16, const RowParams& p, int64_t nvec, cud
     }                                                                                             \
     return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;                       \
   }
-  B200K_TV(32, 4) B200K_TV(32, 8) B200K_TV(32, 16)
+  B200K_TV(32, 3) B200K_TV(32, 4) B200K_TV(32, 6) B200K_TV(32, 8) B200K_TV(32, 12) B200K_TV(32, 16)
   B200K_TV(64, 4) B200K_TV(64, 8) B200K_TV(64, 16)
   B200K_TV(128, 4) B200K_TV(128, 8) B200K_TV(128, 16)
   B200K_TV(256, 4) B200K_TV(256, 8) B200K_TV(256, 16)
