@@ -41,6 +41,27 @@ def test_library_answers_without_gpu():
     assert lib.b200k_gemm_config_info(n, None, None, None, None) == 1  # B200K_ERR_ARG
 
 
+def test_tile_config_pick_rules():
+    """The picker's documented domains (no GPU needed: 148 SMs assumed):
+    CTA-pair tiles only from K = 1536, the 256 x 512 pair tile only from
+    K = 12288, and a config inside the table for every shape."""
+    lib = cabi.library()
+    n = lib.b200k_gemm_num_configs()
+    bm, bn = ctypes.c_int(), ctypes.c_int()
+    info = {}
+    for c in range(n):
+        assert lib.b200k_gemm_config_info(c, ctypes.byref(bm), ctypes.byref(bn), None, None) == 0
+        info[c] = (bm.value, bn.value)
+    for M, N, K in [(12608, 3072, 768), (12608, 2304, 768), (12608, 768, 768), (4096, 4096, 1024), (512, 512, 512),
+                    (1, 8, 8), (16384, 4096, 1535)]:
+        c = lib.b200k_gemm_pick_config(M, N, K)
+        assert 0 <= c < n and info[c][0] == 128, (M, N, K, c)
+    for M, N, K in [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 2048, 2048)]:
+        c = lib.b200k_gemm_pick_config(M, N, K)
+        assert info[c] == (256, 256), (M, N, K, c)
+    assert info[lib.b200k_gemm_pick_config(16384, 4096, 14336)] == (256, 512)
+
+
 def test_host_side_errors_need_no_gpu():
     """Argument errors are caught before any CUDA call."""
     lib = cabi.library()

@@ -7,8 +7,8 @@ to ATen, where cuDNN runs it as an implicit-GEMM convolution with layout
 conversions around it.  This pass rewrites the node as ATen ops the rest of
 the backend already handles:
 
-    x [B, C, H, W] -> view [B, C, Hp, k, Wp, k] -> permute
-      -> b200.pointwise copy -> view [B*Hp*Wp, C*k*k]   (im2col, one copy)
+    x [B, C, H, W] -> view [B, C, Hp, k, Wp, k] -> permute -> contiguous
+      -> view [B*Hp*Wp, C*k*k]                          (im2col, one copy)
     addmm(bias, patches, w.view(OC, C*k*k).t())         (a tensor-core GEMM)
     -> view [B, Hp, Wp, OC] -> permute -> contiguous -> [B, OC, Hp, Wp]
 
@@ -19,23 +19,15 @@ is the patch-embedding idiom `flatten(2).transpose(1, 2)` (a view to
 [B*Hp*Wp, OC] output already is that token-major tensor: the transpose's
 users get a view of it, and neither the NCHW copy nor the strided read of a
 transposed view downstream (ViT's class-token concatenation) remains.  The
-GEMM is then a candidate for the epilogue pass like any other addmm.  The
-im2col copy is a rank-6 permute whose innermost run is one kernel row (k
-contiguous elements); the library's pointwise kernel copies it with 16-byte
-vectors where ATen's generic permute copy does not.
+GEMM is then a candidate for the epilogue pass like any other addmm.
 """
 from __future__ import annotations
 
 import torch
 import torch.fx as fx
 
-from compiler import runtime
-
 from . import config
-from .fusion_pointwise import _tensor_meta, new_kernel_name
-from .program import OP
-
-runtime.load()
+from .fusion_pointwise import _tensor_meta
 
 aten = torch.ops.aten
 
@@ -112,13 +104,11 @@ def fuse_patchify(gm: fx.GraphModule) -> fx.GraphModule:
         if m is None:
             continue
         x, w, b, (bsz, c, hp, kh, wp, kw, oc) = m
-        dtype = _tensor_meta(x).dtype
         tok = _token_major_use(conv, bsz, oc, hp * wp)
         with gm.graph.inserting_before(conv):
             xv = _emit(gm, aten.view.default, [x, [bsz, c, hp, kh, wp, kw]])
             xp = _emit(gm, aten.permute.default, [xv, [0, 2, 4, 1, 3, 5]])
-            xc = _emit(gm, torch.ops.b200.pointwise.default,
-                       [[xp], [OP["MOV"] * 10], [0.0], [bsz, hp, wp, c, kh, kw], dtype])
+            xc = _emit(gm, aten.clone.default, [xp], {"memory_format": torch.contiguous_format})
             a = _emit(gm, aten.view.default, [xc, [bsz * hp * wp, c * kh * kw]])
             w2 = _emit(gm, aten.view.default, [w, [oc, c * kh * kw]])
             wt = _emit(gm, aten.t.default, [w2])
@@ -129,7 +119,6 @@ def fuse_patchify(gm: fx.GraphModule) -> fx.GraphModule:
                 out = _emit(gm, aten.clone.default, [yp], {"memory_format": torch.contiguous_format})
             else:
                 out = _emit(gm, aten.view.default, [y, [bsz, hp * wp, oc]])
-        xc.meta["b200_kernel"] = new_kernel_name("im2col")
         if tok is None:
             out.meta = {**conv.meta, "val": out.meta["val"]}
             conv.replace_all_uses_with(out)

@@ -101,6 +101,7 @@ int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) 
   // for the previous tile's epilogue (~10-20 us): measured on B200, 16384 x
   // 4096 x 14336 with GELU 1410.6 -> 1295.0 us, 8192^3 754.0 -> 759.3 us,
   // 4096^3 106.0 -> 122.6 us, so it is taken only from K = 12288 up.
+  pair_ok = pair_ok && K >= 1536;
   int best = 0;
   double best_cost = 1e300;
   for (int c = 0; c < kNumConfigs; ++c) {
