@@ -398,7 +398,14 @@ def run_single_gemm(args, dist: Dist) -> dict:
     if args.interpret:
         form = []
     w, b = blk.lin.weight, blk.lin.bias
-    if args.tile_config >= 0:
+    if args.plain:  # out = x w^T alone, against torch.mm (cuBLAS) in the eager leg
+        from compiler.optimization.program import OP
+
+        code, imm, form = [OP["MOV"] * 10], [0.0], [1, -1, 0, -1, -1, -1]
+
+        def call():
+            return torch.ops.b200.gemm_epilogue(x, w.t(), [], code, imm, [M, N], torch.bfloat16, form)
+    elif args.tile_config >= 0:
         from compiler.runtime import cabi
 
         out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
@@ -431,11 +438,13 @@ def run_single_gemm(args, dist: Dist) -> dict:
     ms = statistics.median(times)
     # the same block in eager PyTorch (cuBLAS addmm + ATen epilogue kernels)
     with torch.no_grad():
-        eager_ms = statistics.median(_time_device(lambda: blk(x, r), args.steps, args.warmup, flush))
+        eager = (lambda: torch.mm(x, w.t())) if args.plain else (lambda: blk(x, r))
+        eager_ms = statistics.median(_time_device(eager, args.steps, args.warmup, flush))
     return {"metric": "fused GEMM+epilogue TFLOP/s", "value": round(2.0 * M * N * K / (ms * 1e-3) / 1e12, 1),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": "gemm_epilogue", "M": M, "N": N, "K": K, "act": args.act,
+            "config": {"workload": "gemm" if args.plain else "gemm_epilogue", "M": M, "N": N, "K": K,
+                       "act": "none (no epilogue)" if args.plain else args.act,
                        "tile_config": args.tile_config, "program_len": len(code),
                        "epilogue_path": "compiled" if form else "interpreted"},
             "back_to_back_us_per_call": round(wall_us, 1),
@@ -624,6 +633,8 @@ def main() -> None:
     ap.add_argument("--act", default="gelu", choices=ACTS, help="epilogue activation for --workload gemm")
     ap.add_argument("--tile-config", type=int, default=-1, help="force a GEMM tile config (gemm workload)")
     ap.add_argument("--interpret", action="store_true", help="gemm workload: interpret the epilogue program")
+    ap.add_argument("--plain", action="store_true",
+                    help="gemm workload: out = x w^T with no epilogue, against torch.mm in the eager leg")
     ap.add_argument("--cpu-rows", type=int, default=256)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

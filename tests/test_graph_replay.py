@@ -1,0 +1,131 @@
+"""CUDA-graph replay of compiled inference graphs (compiler/graph_replay.py):
+the decision logic on CPU, and op-by-op equality of replayed results on the
+GPU."""
+import pytest
+import torch
+import torch.fx as fx
+import torch.nn as nn
+
+from compiler import graph_replay
+from compiler.optimization import config
+
+DEV = "cuda"
+
+
+def _chain(n_ops: int) -> fx.GraphModule:
+    """x -> (view, relu) repeated: n_ops launching nodes and n_ops views."""
+    g = fx.Graph()
+    x = g.placeholder("x")
+    for _ in range(n_ops):
+        v = g.call_function(torch.ops.aten.view.default, (x, [-1]))
+        x = g.call_function(torch.ops.aten.relu.default, (v,))
+    g.output((x,))
+    return fx.GraphModule(nn.Module(), g)
+
+
+def test_launching_nodes_skip_views():
+    assert graph_replay.launching_nodes(_chain(5)) == 5
+
+
+def test_wrap_replays_only_graphs_with_enough_launches():
+    fn = lambda args: args  # noqa: E731
+    assert graph_replay.wrap(_chain(config.GRAPH_MIN_LAUNCHES - 1), fn) is fn
+    r = graph_replay.wrap(_chain(config.GRAPH_MIN_LAUNCHES), fn)
+    assert isinstance(r, graph_replay.GraphReplay) and r._boxed_call
+
+
+def test_wrap_leaves_graphs_with_large_outputs_op_by_op():
+    fn = lambda args: args  # noqa: E731
+    gm = _chain(config.GRAPH_MIN_LAUNCHES)
+    out = [n for n in gm.graph.nodes if n.op == "output"][0].args[0][0]
+    out.meta["val"] = torch.empty(config.GRAPH_MAX_OUTPUT_MB * 2**20 // 2 + 1, dtype=torch.bfloat16, device="meta")
+    assert graph_replay.output_bytes(gm) > config.GRAPH_MAX_OUTPUT_MB * 2**20
+    assert graph_replay.wrap(gm, fn) is fn
+    out.meta["val"] = torch.empty(64, 1000, dtype=torch.bfloat16, device="meta")
+    assert isinstance(graph_replay.wrap(gm, fn), graph_replay.GraphReplay)
+
+
+def test_cpu_inputs_run_op_by_op():
+    calls = []
+
+    def fn(args):
+        calls.append(1)
+        return [args[0] + 1]
+
+    r = graph_replay.GraphReplay(fn)
+    for _ in range(3):
+        (y,) = r([torch.ones(3)])
+        assert torch.equal(y, torch.full((3,), 2.0))
+    assert len(calls) == 3 and r.graph is None and r.replays == 0
+
+
+class _Blocks(nn.Module):
+    """Pre-norm MLP blocks with residuals: well over 16 launches per call."""
+
+    def __init__(self, dim=256, depth=6):
+        super().__init__()
+        self.norms = nn.ModuleList(nn.LayerNorm(dim) for _ in range(depth))
+        self.up = nn.ModuleList(nn.Linear(dim, 4 * dim) for _ in range(depth))
+        self.down = nn.ModuleList(nn.Linear(4 * dim, dim) for _ in range(depth))
+
+    def forward(self, x):
+        for n, u, d in zip(self.norms, self.up, self.down):
+            x = x + d(torch.nn.functional.gelu(u(n(x))))
+        return x
+
+
+@pytest.mark.gpu
+def test_replayed_graph_matches_op_by_op_and_outputs_survive_later_calls():
+    """Five calls with fresh inputs: the first runs op by op, the second
+    records, the rest replay.  Every result equals the op-by-op compiled
+    function's on the same input bit for bit, and a result taken earlier is
+    not overwritten by later calls (outputs are cloned out of the graph)."""
+    from compiler.backend import custom_backend
+
+    torch.manual_seed(0)
+    model = _Blocks().to(DEV, torch.bfloat16).eval()
+    xs = [torch.randn(512, 256, device=DEV, dtype=torch.bfloat16) for _ in range(5)]
+    torch._dynamo.reset()
+    before = graph_replay.REPLAYS
+    with torch.no_grad():
+        f = torch.compile(model, backend=custom_backend)
+        outs = [f(x) for x in xs]
+        kept = [o.clone() for o in outs]
+        f(torch.randn(512, 256, device=DEV, dtype=torch.bfloat16))
+    torch.cuda.synchronize()
+    assert graph_replay.REPLAYS - before >= 4  # calls 2-5 and the extra call
+    for o, k in zip(outs, kept):
+        assert torch.equal(o, k)
+    old = config.CUDA_GRAPHS
+    try:
+        config.CUDA_GRAPHS = False
+        torch._dynamo.reset()
+        with torch.no_grad():
+            g = torch.compile(model, backend=custom_backend)
+            want = [g(x) for x in xs]
+    finally:
+        config.CUDA_GRAPHS = old
+        torch._dynamo.reset()
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)
+
+
+@pytest.mark.gpu
+def test_replay_reads_parameters_in_place():
+    """A parameter changed in place between calls is seen by the replay (the
+    graph reads parameters from their own storage)."""
+    from compiler.backend import custom_backend
+
+    torch.manual_seed(1)
+    model = _Blocks(depth=4).to(DEV, torch.bfloat16).eval()
+    x = torch.randn(256, 256, device=DEV, dtype=torch.bfloat16)
+    torch._dynamo.reset()
+    with torch.no_grad():
+        f = torch.compile(model, backend=custom_backend)
+        for _ in range(3):
+            f(x)
+        model.down[0].bias.add_(1.0)
+        got = f(x)
+        want = model(x)
+    torch._dynamo.reset()
+    torch.testing.assert_close(got.float(), want.float(), rtol=5e-2, atol=5e-2)

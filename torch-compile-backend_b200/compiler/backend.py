@@ -17,7 +17,7 @@ from torch._decomp import get_decompositions
 from torch._dynamo.backends.common import aot_autograd
 from torch._functorch.aot_autograd import make_boxed_func
 
-from compiler import runtime
+from compiler import graph_replay, runtime
 from compiler.optimization import config
 from compiler.optimization.fusion_epilogue import fuse_epilogue
 from compiler.optimization.fusion_patchify import fuse_patchify
@@ -37,7 +37,7 @@ def _dump(gm: fx.GraphModule) -> None:
                 print(f"#   program: {n.meta['b200_program']}")
 
 
-def compiler(gm: fx.GraphModule, example_inputs):
+def _passes(gm: fx.GraphModule) -> fx.GraphModule:
     if config.EXTENSIONS and config.ENABLE_PATCHIFY:
         gm = fuse_patchify(gm)  # patch-embedding convolutions -> im2col + addmm (extension)
     if config.EXTENSIONS and config.ENABLE_ROWREDUCE:
@@ -52,12 +52,29 @@ def compiler(gm: fx.GraphModule, example_inputs):
         gm = fuse_pointwise(gm)  # the remaining pointwise groups
     if config.DUMP:
         _dump(gm)
-    return make_boxed_func(gm.forward)
+    return gm
+
+
+def compiler(gm: fx.GraphModule, example_inputs):
+    """Forward and backward graphs of training: the passes, run op by op."""
+    return make_boxed_func(_passes(gm).forward)
+
+
+def inference_compiler(gm: fx.GraphModule, example_inputs):
+    """Inference graphs (no input requires grad): the passes, then CUDA-graph
+    replay when the graph launches enough kernels (compiler/graph_replay.py;
+    an extension, B200_CUDA_GRAPHS=0 turns it off)."""
+    gm = _passes(gm)
+    fn = make_boxed_func(gm.forward)
+    if config.EXTENSIONS:
+        fn = graph_replay.wrap(gm, fn)
+    return fn
 
 
 custom_backend = aot_autograd(
     fw_compiler=compiler,
     bw_compiler=compiler,
+    inference_compiler=inference_compiler,
     decompositions=get_decompositions([torch.ops.aten.gelu, torch.ops.aten.silu]),
 )
 

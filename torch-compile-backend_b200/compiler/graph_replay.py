@@ -1,0 +1,173 @@
+"""CUDA-graph replay of compiled inference graphs (an extension: the
+reference runs every compiled graph op by op from Python).
+
+A compiled forward graph of a model issues one kernel launch per fused group
+and per remaining ATen op: 195 launches for the Llama-style prefill, 90 for
+ViT-B/16.  Run op by op, the host side of those calls leaves the GPU idle
+between kernels (the Llama prefill: 31.4 ms of kernels in a 36.2 ms forward).
+``GraphReplay`` records the graph's launches once into a CUDA graph and
+replays it, so one host call issues all of them.
+
+Semantics are those of the op-by-op function:
+  * inputs: tensors that are the same storage at every call (parameters,
+    module buffers) are read in place; every other tensor input is copied
+    into the graph's own input buffer before each replay;
+  * outputs: each replay's outputs are cloned out of the graph's buffers, so
+    a result stays valid after later calls;
+  * the first call runs op by op (it also warms up lazily initialised
+    libraries); the second records the graph; any failure to record, and any
+    call whose inputs no longer match the recording (another device, shape,
+    dtype or stride, or a moved parameter), runs op by op instead.
+The graph's intermediate buffers stay allocated (in a private memory pool)
+for the life of the compiled function.  Only inference graphs with at least
+``config.GRAPH_MIN_LAUNCHES`` launching nodes and CUDA inputs take this path;
+training graphs, whose forward outputs are saved for the backward pass, do
+not.  A graph whose outputs exceed ``config.GRAPH_MAX_OUTPUT_MB`` runs op by
+op: cloning them costs more than replay saves (measured on B200: ViT-B/16,
+90 launches and a [64, 1000] output, 3.142 -> 2.998 ms per forward; the
+Llama-style prefill, 195 launches of mostly long GEMMs and a 4.2 GB logits
+output, 37.17 -> 38.36 ms).
+"""
+from __future__ import annotations
+
+import torch
+import torch.fx as fx
+
+from compiler.optimization import config
+
+aten = torch.ops.aten
+
+# Replays issued by every GraphReplay of this process (a diagnostic count).
+REPLAYS = 0
+
+# Nodes that never launch a kernel (views, metadata, Python-level getitem).
+_NO_LAUNCH = {
+    aten.view.default, aten._unsafe_view.default, aten.reshape.default, aten.t.default, aten.transpose.int,
+    aten.permute.default, aten.expand.default, aten.unsqueeze.default, aten.squeeze.dim, aten.squeeze.default,
+    aten.slice.Tensor, aten.select.int, aten.split.Tensor, aten.split_with_sizes.default, aten.unbind.int,
+    aten.alias.default, aten.detach.default, aten.as_strided.default, aten.sym_size.int, aten.sym_stride.int,
+}
+
+
+def launching_nodes(gm: fx.GraphModule) -> int:
+    """Number of call_function nodes that launch work on the GPU."""
+    n = 0
+    for node in gm.graph.nodes:
+        if node.op != "call_function" or node.target in _NO_LAUNCH:
+            continue
+        if getattr(node.target, "__name__", "") == "getitem":
+            continue
+        n += 1
+    return n
+
+
+def _is_persistent(t: torch.Tensor) -> bool:
+    """A parameter or a leaf that requires grad: the same storage every call."""
+    return isinstance(t, torch.nn.Parameter) or (t.requires_grad and t.is_leaf)
+
+
+class GraphReplay:
+    """Boxed callable: ``run(args)`` with ``args`` the graph's input list."""
+
+    _boxed_call = True  # AOTAutograd's marker for the list-argument calling convention
+
+    def __init__(self, fn):
+        self.fn = fn  # boxed op-by-op function of the compiled graph
+        self.calls = 0
+        self.replays = 0
+        self.graph = None
+        self.disabled = False
+        self.static_in = None
+        self.persistent = None
+        self.sig = None
+        self.static_out = None
+        self.ptrs = None
+
+    @staticmethod
+    def _signature(args):
+        return [(a.device, a.dtype, tuple(a.shape), tuple(a.stride())) if isinstance(a, torch.Tensor) else a
+                for a in args]
+
+    def _eligible(self, args) -> bool:
+        tensors = [a for a in args if isinstance(a, torch.Tensor)]
+        if not tensors or not all(t.is_cuda for t in tensors):
+            return False
+        dev = tensors[0].device
+        return all(t.device == dev for t in tensors) and all(
+            isinstance(a, (torch.Tensor, int, float, bool, type(None))) for a in args)
+
+    def _record(self, args):
+        self.persistent = [isinstance(a, torch.Tensor) and _is_persistent(a) for a in args]
+        self.static_in = [a if (not isinstance(a, torch.Tensor) or p) else a.clone()
+                          for a, p in zip(args, self.persistent)]
+        self.sig = self._signature(args)
+        self.ptrs = [a.data_ptr() if p else None for a, p in zip(args, self.persistent)]
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            self.fn(list(self.static_in))  # warm-up on the side stream, as graph capture requires
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            outs = self.fn(list(self.static_in))
+        outs = list(outs) if isinstance(outs, (list, tuple)) else [outs]
+        storages = {a.untyped_storage().data_ptr() for a in self.static_in if isinstance(a, torch.Tensor)}
+        if any(isinstance(o, torch.Tensor) and o.untyped_storage().data_ptr() in storages for o in outs):
+            raise RuntimeError("an output aliases an input")
+        out_bytes = sum(o.numel() * o.element_size() for o in outs if isinstance(o, torch.Tensor))
+        if out_bytes > config.GRAPH_MAX_OUTPUT_MB * 2**20:
+            raise RuntimeError("outputs too large to clone per call")
+        self.graph, self.static_out = graph, outs
+
+    def _matches(self, args) -> bool:
+        if self._signature(args) != self.sig:
+            return False
+        return all(p is None or a.data_ptr() == p for a, p in zip(args, self.ptrs))
+
+    def __call__(self, args):
+        self.calls += 1
+        if self.disabled or not self._eligible(args):
+            return self.fn(args)
+        if self.graph is None:
+            if self.calls == 1:
+                return self.fn(args)  # op by op: warms up lazily initialised libraries
+            try:
+                self._record(args)
+            except Exception:  # recording is an optimisation: fall back for good
+                self.disabled = True
+                self.graph = None
+                return self.fn(args)
+        if not self._matches(args):
+            return self.fn(args)
+        for a, s, p in zip(args, self.static_in, self.persistent):
+            if isinstance(a, torch.Tensor) and not p and a.data_ptr() != s.data_ptr():
+                s.copy_(a)
+        self.graph.replay()
+        self.replays += 1
+        global REPLAYS
+        REPLAYS += 1
+        return [o.clone() if isinstance(o, torch.Tensor) else o for o in self.static_out]
+
+
+def output_bytes(gm: fx.GraphModule) -> int:
+    """Bytes of the graph's tensor outputs, from the traced metadata."""
+    total = 0
+    for node in gm.graph.nodes:
+        if node.op != "output":
+            continue
+        outs = node.args[0] if isinstance(node.args[0], (list, tuple)) else [node.args[0]]
+        for o in outs:
+            v = o.meta.get("val") if isinstance(o, fx.Node) else None
+            if isinstance(v, torch.Tensor):
+                total += v.numel() * v.element_size()
+    return total
+
+
+def wrap(gm: fx.GraphModule, boxed_fn):
+    """The boxed function of an inference graph, replayed as a CUDA graph when
+    it launches enough kernels to gain from it and its outputs are small
+    enough to clone per call; otherwise `boxed_fn`."""
+    if (not config.CUDA_GRAPHS or launching_nodes(gm) < config.GRAPH_MIN_LAUNCHES
+            or output_bytes(gm) > config.GRAPH_MAX_OUTPUT_MB * 2**20):
+        return boxed_fn
+    return GraphReplay(boxed_fn)

@@ -11,6 +11,13 @@ Environment flags (read once at import, overridable as module attributes):
   B200_PATCHIFY=0     keep patch-embedding convolutions as convolutions
   B200_DUMP=1         print each compiled graph and the fused-kernel programs
   B200_FAST_EPILOGUE=0  always interpret GEMM epilogue programs
+  B200_CUDA_GRAPHS=0  run compiled inference graphs op by op instead of
+                      replaying them as CUDA graphs (compiler/graph_replay.py)
+  B200_GRAPH_MIN_LAUNCHES=N  replay only graphs with at least N launching
+                      nodes (default 16: one GEMM gains nothing from replay
+                      but would pay the input and output copies)
+  B200_GRAPH_MAX_OUTPUT_MB=N  replay only graphs whose outputs, cloned after
+                      every replay, total at most N MiB (default 64)
 
 The reference hard-codes its equivalents (AUTOTUNE_CONFIGS, BLOCK=1024,
 DOT_DTYPES in compiler/optimization/fusion_epilogue.py:23-38 and
@@ -37,6 +44,9 @@ ENABLE_ROPE = _flag("B200_ROPE", True)
 ENABLE_PATCHIFY = _flag("B200_PATCHIFY", True)
 DUMP = _flag("B200_DUMP", False)
 FAST_EPILOGUE = _flag("B200_FAST_EPILOGUE", True)  # compiled path for canonical GEMM epilogues
+CUDA_GRAPHS = _flag("B200_CUDA_GRAPHS", True)  # replay compiled inference graphs as CUDA graphs
+GRAPH_MIN_LAUNCHES = int(os.environ.get("B200_GRAPH_MIN_LAUNCHES", "16"))
+GRAPH_MAX_OUTPUT_MB = int(os.environ.get("B200_GRAPH_MAX_OUTPUT_MB", "64"))
 
 # Kernel library limits (include/b200k.h).
 MAX_INPUTS = 8
