@@ -59,6 +59,12 @@ constexpr int UMMA_K = 16;
 // tiles on 148 SMs, 8 for the 74 CTA pairs of 256-row tiles.
 constexpr int kGroupM = 16;
 constexpr int kGroupMPair = 8;
+// The MMA thread signals tsoon[acc] this many K blocks before a tile's last
+// one (~5 us at B200 MMA rates), and the epilogue warps then warm L2 with the
+// tile's full-matrix operand rows (residual / scale).  Warmed one whole tile
+// earlier, as first done, those rows were evicted again by the operand
+// streams of large GEMMs before the epilogue read them.
+constexpr int kSoonBlocks = 12;
 
 // Epilogue warp layout of a BN-wide tile: NG column groups of CW columns,
 // one warp per (TMEM lane quarter, column group); warps 0-3 are control.
@@ -635,8 +641,9 @@ __device__ __forceinline__ void prefetch_l2(const void* ptr) {
 
 // Warms L2 with this lane's row of the full-matrix operand (residual or
 // scale) for the tile at (m, n): the warp's CW columns, which the
-// sub-chunks later read straight into registers.  Issued one tile ahead, so
-// those reads wait on L2 rather than DRAM.
+// sub-chunks later read straight into registers.  Issued when the MMA
+// thread signals that the tile is kSoonBlocks K blocks from done, so those
+// reads wait on L2 rather than DRAM.
 template <int CW, int ROW>
 __device__ __forceinline__ void prefetch_row16_l2(const Params& p, int m, int n) {
   if (ROW == ROW_NONE || m >= p.M || n >= p.N) return;
@@ -791,8 +798,9 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
 // next tile's MMAs into half 0 start while half 1 is still being drained.
 template <int BN, int OUT_BYTES, int ACT, int ROW, bool PAIR = false, bool WIDE = false>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
-                                                   uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
-                                                   int cg, int lane, const Ctl& ctl, uint32_t rank = 0) {
+                                                   uint64_t* tfull, uint64_t* tempty, uint64_t* tsoon, uint8_t* sb,
+                                                   int quarter, int cg, int lane, const Ctl& ctl,
+                                                   uint32_t rank = 0) {
   static_assert(PAIR || !WIDE, "wide tiles run on CTA pairs");
   constexpr int CW = Epi<BN>::CW;
   constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and accumulator half
@@ -806,9 +814,6 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
   if (t0 < p.num_tiles) {
     int tm, tn;
     tile_coords(t0, p, tm, tn);
-#pragma unroll
-    for (int h = 0; h < H; ++h)
-      prefetch_row16_l2<CW, ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + h * BN + cg * CW);
     fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + cg * CW, cur);
   }
   int acc = 0;
@@ -825,8 +830,19 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       tile_coords(t + step, p, tm2, tn2);
       m2 = tm2 * TM + rank_rows + quarter * 32 + lane;
       n2 = tn2 * TN + cg * CW;
+    }
+    if constexpr (ROW != ROW_NONE) {
+      // a few K blocks before the accumulator is ready: warm L2 with this
+      // lane's row of the operand for the whole tile (in a pair, the even
+      // CTA's warps warm both CTAs' rows; the odd CTA has no signal)
+      if (!PAIR || rank == 0) {
+        if (!wait_bar(&tsoon[acc], aph, ctl)) break;
 #pragma unroll
-      for (int h = 0; h < H; ++h) prefetch_row16_l2<CW, ROW>(p, m2, n2 + h * BN);
+        for (int h = 0; h < H; ++h)
+#pragma unroll
+          for (int r = 0; r < (PAIR ? 2 : 1); ++r)
+            prefetch_row16_l2<CW, ROW>(p, tm * TM + r * BM + quarter * 32 + lane, tn * TN + h * BN + cg * CW);
+      }
     }
     if (!wait_bar(&tfull[acc], aph, ctl)) break;
     tc_fence_after();
@@ -899,7 +915,8 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tsoon = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsoon + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -916,6 +933,7 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
       mbar_init(&tempty[a], Epi<BN>::kWarps);
     }
     mbar_init(drain, 1);
+    for (int a = 0; a < 2; ++a) mbar_init(&tsoon[a], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1008,6 +1026,7 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
             umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
+          if (kb == max(0, p.k_blocks - kSoonBlocks)) mbar_arrive(&tsoon[acc]);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
@@ -1030,8 +1049,8 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
     if constexpr (FAST) {
     // ------------------------------------------------------------ epilogue (compiled form)
     const int ew = warp - 4;
-    epilogue_fast_loop<BN, OUT_BYTES, ACT, ROW>(p, &tmO, tmem_base, tfull, tempty, sStg + ew * kStgBytes, warp & 3,
-                                                ew >> 2, lane, ctl);
+    epilogue_fast_loop<BN, OUT_BYTES, ACT, ROW>(p, &tmO, tmem_base, tfull, tempty, tsoon, sStg + ew * kStgBytes,
+                                                warp & 3, ew >> 2, lane, ctl);
     } else {
     // ------------------------------------------------------------ epilogue (interpreted program)
     // Warp w reads TMEM lane quarter (w % 4) and one half of the tile's columns.
@@ -1153,7 +1172,8 @@ __global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
   uint64_t* drain = tempty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* tsoon = drain + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tsoon + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t rank = cluster_rank();
@@ -1172,6 +1192,7 @@ __global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
       mbar_init(&tempty[a], 2 * Epi<kPairMmaN>::kWarps);
     }
     mbar_init(drain, 1);
+    for (int a = 0; a < 2; ++a) mbar_init(&tsoon[a], 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -1273,6 +1294,11 @@ __global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
           if (!ok) break;
           umma_commit_pair(smem_u32(&empty[s]));
           umma_commit_pair(cluster_addr(&empty[s], 1));
+          // Local only: the even CTA's epilogue warms L2 for both CTAs' rows.
+          // Signalling the odd CTA as well cost MMA issue time (measured on
+          // 8192^3: a remote mbarrier arrive from this thread 701 -> 967 us,
+          // two extra commits 722 -> 777 us).
+          if (kb == max(0, p.k_blocks - kSoonBlocks)) mbar_arrive(&tsoon[acc]);
           if (++s == STAGES) {
             s = 0;
             ph ^= 1u;
@@ -1297,7 +1323,7 @@ __global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int ew = warp - 4;
-    epilogue_fast_loop<kPairMmaN, OUT_BYTES, ACT, ROW, true, WIDE>(p, &tmO, tmem_base, tfull, tempty,
+    epilogue_fast_loop<kPairMmaN, OUT_BYTES, ACT, ROW, true, WIDE>(p, &tmO, tmem_base, tfull, tempty, tsoon,
                                                                    sStg + ew * kStgBytes, warp & 3, ew >> 2, lane,
                                                                    ctl, rank);
   }
