@@ -141,14 +141,14 @@ __device__ __forceinline__ void store_vec8(void* base, int64_t off, int dt, cons
 constexpr int kSlots = B200K_MAX_SLOTS;
 
 #define B200K_BIN_CASES(OPC, EXPR)                                                  \
-  case OPC * 10 + 0: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[0][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 1: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[1][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 2: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[2][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 3: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[3][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 4: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[4][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 5: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[5][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 6: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[6][j]; acc[j] = (EXPR); } } break; \
-  case OPC * 10 + 7: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[7][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 0: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[0 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 1: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[1 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 2: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[2 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 3: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[3 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 4: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[4 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 5: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[5 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 6: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[6 % S][j]; acc[j] = (EXPR); } } break; \
+  case OPC * 10 + 7: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = r[7 % S][j]; acc[j] = (EXPR); } } break; \
   case OPC * 10 + 8: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { float a = acc[j], x = imm; acc[j] = (EXPR); } } break;
 
 #define B200K_UN_CASE(OPC, EXPR) \
@@ -157,32 +157,35 @@ constexpr int kSlots = B200K_MAX_SLOTS;
 #define B200K_SLOT_CASE(OPC, S, BODY) \
   case OPC * 10 + S: { _Pragma("unroll") for (int j = 0; j < VEC; ++j) { BODY; } } break;
 
-template <int VEC>
-__device__ __forceinline__ void run_program(const B200kProgram& prog, float (&r)[kSlots][VEC], float (&acc)[VEC]) {
+// S < kSlots: a kernel that keeps only S slots in registers; programs it runs
+// name no slot >= S (the host checks, slots_used()), so the cases that would
+// (slot k maps to k % S) are never taken.
+template <int VEC, int S = kSlots>
+__device__ __forceinline__ void run_program(const B200kProgram& prog, float (&r)[S][VEC], float (&acc)[VEC]) {
   const int n = prog.n;
   for (int pc = 0; pc < n; ++pc) {
     const int code = prog.ins[pc].code;
     const float imm = prog.ins[pc].imm;
     switch (code) {
       // acc = slot / imm
-      B200K_SLOT_CASE(B200K_OP_MOV, 0, acc[j] = r[0][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 1, acc[j] = r[1][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 2, acc[j] = r[2][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 3, acc[j] = r[3][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 4, acc[j] = r[4][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 5, acc[j] = r[5][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 6, acc[j] = r[6][j])
-      B200K_SLOT_CASE(B200K_OP_MOV, 7, acc[j] = r[7][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 0, acc[j] = r[0 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 1, acc[j] = r[1 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 2, acc[j] = r[2 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 3, acc[j] = r[3 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 4, acc[j] = r[4 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 5, acc[j] = r[5 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 6, acc[j] = r[6 % S][j])
+      B200K_SLOT_CASE(B200K_OP_MOV, 7, acc[j] = r[7 % S][j])
       B200K_SLOT_CASE(B200K_OP_MOV, 8, acc[j] = imm)
       // slot = acc
-      B200K_SLOT_CASE(B200K_OP_STORE, 0, r[0][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 1, r[1][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 2, r[2][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 3, r[3][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 4, r[4][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 5, r[5][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 6, r[6][j] = acc[j])
-      B200K_SLOT_CASE(B200K_OP_STORE, 7, r[7][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 0, r[0 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 1, r[1 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 2, r[2 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 3, r[3 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 4, r[4 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 5, r[5 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 6, r[6 % S][j] = acc[j])
+      B200K_SLOT_CASE(B200K_OP_STORE, 7, r[7 % S][j] = acc[j])
       B200K_BIN_CASES(B200K_OP_ADD, a + x)
       B200K_BIN_CASES(B200K_OP_SUB, a - x)
       B200K_BIN_CASES(B200K_OP_RSUB, x - a)

@@ -26,6 +26,18 @@ inline int dtype_size(int dt) {
 }
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Slots a (validated) program touches: the loaded operands and every slot an
+// instruction names.
+inline int slots_used(const B200kProgram& prog, int n_loaded) {
+  int n = n_loaded;
+  for (int i = 0; i < prog.n; ++i) {
+    const int op = prog.ins[i].code / 10, operand = prog.ins[i].code % 10;
+    const bool names_slot = op == B200K_OP_STORE || op == B200K_OP_MOV || (op >= B200K_OP_ADD && op <= B200K_OP_MIN);
+    if (names_slot && operand < B200K_MAX_SLOTS) n = operand + 1 > n ? operand + 1 : n;
+  }
+  return n;
+}
+
 // Checks every instruction of an accumulator-machine program: known opcode,
 // operand kind allowed for that opcode.  `n_loaded` slots hold operands.
 inline int validate_program(const B200kProgram& prog, int n_loaded) {

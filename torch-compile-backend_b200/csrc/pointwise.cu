@@ -109,7 +109,124 @@ __global__ void __launch_bounds__(256) pointwise_kernel(const __grid_constant__ 
   }
 }
 
+// Vector path for the common launches: merged rank 1 or 2, at most four
+// inputs and four program slots, 32-bit unit indices, unit-stride inputs of
+// bf16, f16 or f32.  The
+// generic kernel above serves every launch with one thread-unit of work per
+// loop step and index arithmetic over all six dims and eight input slots
+// (~400 instructions per 8 elements, latency-bound at 2 warps per
+// scheduler: a bf16 add moved ~1 TB/s).  Here the index arithmetic is only
+// that of RANK dims and NIN inputs, and each thread issues the 16-byte loads
+// of U units before it runs the program on the first, so U x NIN loads per
+// thread are in flight.
+constexpr int kFastSlots = 4;  // programs of at most four slots (the host checks)
+// W: 16-byte words of one 8-element unit of every unit-stride input (1: all
+// 16-bit, 2: all f32).
+template <int RANK, int NIN, int U, int W>
+__global__ void __launch_bounds__(256) pointwise_fast_kernel(const __grid_constant__ PwParams p) {
+  const uint32_t total = p.nunits;
+  const uint32_t step = gridDim.x * blockDim.x * U;
+  for (uint32_t base = blockIdx.x * blockDim.x * U + threadIdx.x; base < total; base += step) {
+    uint4 raw[U][NIN][W];
+    int64_t off[U][NIN];
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const uint32_t u = base + k * blockDim.x;
+      if (u >= total) break;
+      uint32_t i0 = 0, i1 = u;
+      if (RANK == 2) {
+        i0 = fdiv(u, p.div[1]);
+        i1 = u - i0 * p.div[1].d;
+      }
+#pragma unroll
+      for (int i = 0; i < NIN; ++i) {
+        off[k][i] = RANK == 2 ? static_cast<int64_t>(i0) * p.strides[i][0] + static_cast<int64_t>(i1) * p.strides[i][1]
+                              : static_cast<int64_t>(i1) * p.strides[i][0];
+        if (p.inner_stride[i] == 1) {
+          const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.in[i]) + off[k][i] * (2 * W));
+#pragma unroll
+          for (int w = 0; w < W; ++w) raw[k][i][w] = __ldg(q + w);
+        }
+      }
+    }
+    // One copy of the program loop (the interpreter is large): unit k's
+    // operands are always in slot 0 of raw/off, shifted down after each unit.
+#pragma unroll 1
+    for (int k = 0; k < U; ++k) {
+      const uint32_t u = base + k * blockDim.x;
+      if (u >= total) break;
+      float r[kFastSlots][8];
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < NIN; ++i) {
+        if (p.inner_stride[i] == 1) {
+          if constexpr (W == 2) {
+            const float* f = reinterpret_cast<const float*>(&raw[0][i][0]);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) r[i][j] = f[j];
+          } else {
+            const uint32_t w[4] = {raw[0][i][0].x, raw[0][i][0].y, raw[0][i][0].z, raw[0][i][0].w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = p.dt[i] == B200K_BF16 ? __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]))
+                                                     : __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+              r[i][2 * j] = f.x;
+              r[i][2 * j + 1] = f.y;
+            }
+          }
+        } else {
+          const float sc = load_scalar(p.in[i], off[0][i], p.dt[i]);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) r[i][j] = sc;
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = r[0][j];
+      run_program<8, kFastSlots>(p.prog, r, acc);
+      store_vec8(p.out, static_cast<int64_t>(u) * 8, p.out_dt, acc);
+#pragma unroll
+      for (int kk = 0; kk + 1 < U; ++kk) {
+#pragma unroll
+        for (int i = 0; i < NIN; ++i) {
+#pragma unroll
+          for (int w = 0; w < W; ++w) raw[kk][i][w] = raw[kk + 1][i][w];
+          off[kk][i] = off[kk + 1][i];
+        }
+      }
+    }
+  }
+}
+
 namespace {
+
+template <int RANK, int NIN, int W>
+int launch_fast(const PwParams& p, int64_t units, cudaStream_t stream) {
+  constexpr int U = NIN * W <= 1 ? 4 : 2;  // units in flight per thread (more spill past ~128 registers)
+  auto kernel = pointwise_fast_kernel<RANK, NIN, U, W>;
+  const int sms = device_sm_count();
+  if (sms <= 0) return B200K_ERR_DEVICE;
+  static int per_sm = 0;  // resident CTAs per SM for this instantiation
+  if (per_sm == 0) {
+    int v = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, kernel, 256, 0) != cudaSuccess) return B200K_ERR_LAUNCH;
+    per_sm = std::max(v, 1);
+  }
+  const int64_t want = (units + 256 * U - 1) / (256 * U);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(sms) * per_sm)));
+  kernel<<<grid, 256, 0, stream>>>(p);
+  return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
+}
+
+template <int RANK, int W>
+int launch_fast_nin(int nin, const PwParams& p, int64_t units, cudaStream_t stream) {
+  switch (nin) {
+    case 1: return launch_fast<RANK, 1, W>(p, units, stream);
+    case 2: return launch_fast<RANK, 2, W>(p, units, stream);
+    case 3: return launch_fast<RANK, 3, W>(p, units, stream);
+    case 4: return launch_fast<RANK, 4, W>(p, units, stream);
+    default: return B200K_ERR_UNSUPPORTED;
+  }
+}
 
 struct Dim {
   int64_t size;
@@ -240,6 +357,20 @@ extern "C" int b200k_pointwise(const B200kPointwiseArgs* a, void* stream_) {
     for (int d = 0; d < nm; ++d) p.div[d] = make_fastdiv(static_cast<uint32_t>(p.sizes[d]));
   }
 
+  if (vec && !i64 && nm <= 2 && nin <= 4 && slots_used(a->program, nin) <= kFastSlots) {
+    int w = 0;  // 16-byte words per unit, the same for every unit-stride input
+    bool fast = true;
+    for (int i = 0; i < nin; ++i) {
+      if (p.inner_stride[i] != 1) continue;
+      const int wi = p.dt[i] == B200K_F32 ? 2 : (p.dt[i] == B200K_BF16 || p.dt[i] == B200K_F16) ? 1 : 0;
+      if (wi == 0 || (w != 0 && wi != w)) fast = false;
+      w = wi;
+    }
+    if (fast && w == 1)
+      return nm == 2 ? launch_fast_nin<2, 1>(nin, p, units, stream) : launch_fast_nin<1, 1>(nin, p, units, stream);
+    if (fast && w == 2)
+      return nm == 2 ? launch_fast_nin<2, 2>(nin, p, units, stream) : launch_fast_nin<1, 2>(nin, p, units, stream);
+  }
   if (vec) return i64 ? launch_grid_stride<8, true>(p, units, stream) : launch_grid_stride<8, false>(p, units, stream);
   return i64 ? launch_grid_stride<1, true>(p, units, stream) : launch_grid_stride<1, false>(p, units, stream);
 }
