@@ -446,6 +446,29 @@ def test_patchify_keeps_the_nchw_layout_for_other_uses():
     assert clones[1].meta["val"].is_contiguous()
 
 
+def test_broadcast_cat_inputs_are_made_contiguous():
+    """ViT's class-token concatenation: the expanded (zero-stride) input of
+    the cat gets a contiguous copy, the token input is left alone, and the
+    values are the same."""
+
+    class ClsCat(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.cls = nn.Parameter(torch.randn(1, 1, 32))
+
+        def forward(self, x):
+            return torch.cat([self.cls.expand(x.shape[0], -1, -1), x], dim=1) * 2
+
+    model = ClsCat().to(torch.bfloat16)
+    x = torch.randn(4, 6, 32).to(torch.bfloat16)
+    (gm,) = fused_graphs(model, (x,))
+    cat = [n for n in gm.graph.nodes if n.target == torch.ops.aten.cat.default][0]
+    first, second = cat.args[0]
+    assert first.target == torch.ops.aten.clone.default and first.args[0].target == torch.ops.aten.expand.default
+    assert first.meta["val"].is_contiguous() and tuple(first.meta["val"].shape) == (4, 1, 32)
+    assert second.target != torch.ops.aten.clone.default
+
+
 def test_patchify_leaves_overlapping_convolutions():
     class Conv(nn.Module):
         def __init__(self):

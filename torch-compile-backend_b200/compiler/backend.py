@@ -19,6 +19,7 @@ from torch._functorch.aot_autograd import make_boxed_func
 
 from compiler import graph_replay, runtime
 from compiler.optimization import config
+from compiler.optimization.cat_inputs import contiguous_cat_inputs
 from compiler.optimization.fusion_epilogue import fuse_epilogue
 from compiler.optimization.fusion_patchify import fuse_patchify
 from compiler.optimization.fusion_pointwise import fuse_pointwise
@@ -40,6 +41,8 @@ def _dump(gm: fx.GraphModule) -> None:
 def _passes(gm: fx.GraphModule) -> fx.GraphModule:
     if config.EXTENSIONS and config.ENABLE_PATCHIFY:
         gm = fuse_patchify(gm)  # patch-embedding convolutions -> im2col + addmm (extension)
+    if config.EXTENSIONS:
+        gm = contiguous_cat_inputs(gm)  # broadcast cat inputs made contiguous (extension)
     if config.EXTENSIONS and config.ENABLE_ROWREDUCE:
         gm = fuse_rowreduce(gm)  # whole row groups (extension; runs first so the
         #                          pointwise passes do not split them)
