@@ -29,7 +29,8 @@ class MLPBlock(nn.Module):
 
 
 class TanhGeluMLP(nn.Module):
-    """The BASELINE CPU configuration's structure: Linear -> tanh-GELU -> Linear -> +x."""
+    """The structure of the reference's CPU MLP benchmark (bench/mlp.py):
+    Linear -> tanh-GELU -> Linear -> +x."""
 
     def __init__(self, dim=32, hidden=64):
         super().__init__()
