@@ -585,6 +585,57 @@ def run_chain(args, dist: Dist) -> dict:
                                          "peak_source": src + " hbm_gbs"}}
 
 
+def run_pointwise(args, dist: Dist) -> dict:
+    """Pointwise chains through the compiled graph (the pointwise pass and
+    `b200k_pointwise`): `(x*sigmoid(x) + r) * w` in bf16 on [16384, 8192]
+    with w [8192], `(a + b) * 0.5` in bf16 on [16384, 8192] and
+    `(a + b) * c` in fp32 on [16384, 4096]; GB/s of algorithmic traffic
+    (every input read once, the output written once)."""
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    class SiluResScale(torch.nn.Module):
+        def forward(self, x, r, w):
+            return (x * torch.sigmoid(x) + r) * w
+
+    class AddHalf(torch.nn.Module):
+        def forward(self, a, b):
+            return (a + b) * 0.5
+
+    class AddMul(torch.nn.Module):
+        def forward(self, a, b, c):
+            return (a + b) * c
+
+    def rnd(*shape, dt=torch.bfloat16):
+        return torch.randn(*shape, device=dev, generator=gen).to(dt)
+
+    cases = (("silu_residual_scale_bf16", SiluResScale(), (rnd(16384, 8192), rnd(16384, 8192), rnd(8192))),
+             ("add_half_bf16", AddHalf(), (rnd(16384, 8192), rnd(16384, 8192))),
+             ("add_mul_f32", AddMul(), tuple(rnd(16384, 4096, dt=torch.float32) for _ in range(3))))
+    be = _backend(args.backend)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    out = {}
+    with torch.no_grad():
+        for name, mod, inp in cases:
+            nbytes = sum(t.numel() * t.element_size() for t in inp) + inp[0].numel() * inp[0].element_size()
+            torch._dynamo.reset()
+            f = mod if be is None else torch.compile(mod, backend=be)
+            times = _time_device(lambda: f(*inp), args.steps, args.warmup, flush)
+            ms = statistics.median(times)
+            out[name] = {"ms": round(ms, 4), "GB/s": round(nbytes / (ms * 1e-3) / 1e9, 1), "bytes": nbytes}
+    peaks, src = load_peaks()
+    tot_bytes = sum(v["bytes"] for v in out.values())
+    tot_ms = sum(v["ms"] for v in out.values())
+    gbs = tot_bytes / (tot_ms * 1e-3) / 1e9
+    return {"metric": "pointwise chain GB/s", "value": round(gbs, 1), "unit": "GB/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(tot_ms, 4), "higher_is_better": True,
+            "dtype": "bf16+fp32", "data": "synthetic", "config": {"workload": "pointwise_chains", "backend": args.backend},
+            "kernels": out, "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peaks["hbm_gbs"],
+                                         "unit": "GB/s", "frac": round(gbs / peaks["hbm_gbs"], 3),
+                                         "peak_source": src + " hbm_gbs"}}
+
+
 # --------------------------------------------------------------- CPU (oracle) leg
 def cpu_sweep(rows: int, reps: int) -> dict:
     """The oracle's GEMM + epilogue (numpy fp32, every host core via BLAS) on
@@ -625,7 +676,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm", "vit", "llama", "chain"])
+    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm", "vit", "llama", "chain", "pointwise"])
     ap.add_argument("--backend", default="ours", choices=["ours", "eager", "reference_triton", "inductor"],
                     help="vit/llama/chain workloads: which torch.compile backend runs the model")
     ap.add_argument("--batch", type=int, default=0, help="vit/llama batch (default: the benchmark config)")
@@ -665,6 +716,9 @@ def main() -> None:
             return
         if args.workload == "chain":
             print(json.dumps(run_chain(args, dist)))
+            return
+        if args.workload == "pointwise":
+            print(json.dumps(run_pointwise(args, dist)))
             return
         res = run_sweep(args, dist)
         if dist.rank == 0:

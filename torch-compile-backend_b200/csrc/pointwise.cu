@@ -128,29 +128,33 @@ __global__ void __launch_bounds__(256) pointwise_fast_kernel(const __grid_consta
   const uint32_t step = gridDim.x * blockDim.x * U;
   for (uint32_t base = blockIdx.x * blockDim.x * U + threadIdx.x; base < total; base += step) {
     uint4 raw[U][NIN][W];
-    int64_t off[U][NIN];
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-      const uint32_t u = base + k * blockDim.x;
-      if (u >= total) break;
+    // Element offset of input i at unit u (recomputed where needed rather
+    // than kept per unit: registers go to the loads in flight).
+    auto offset = [&](uint32_t u, int i) -> int64_t {
       uint32_t i0 = 0, i1 = u;
       if (RANK == 2) {
         i0 = fdiv(u, p.div[1]);
         i1 = u - i0 * p.div[1].d;
       }
+      return RANK == 2 ? static_cast<int64_t>(i0) * p.strides[i][0] + static_cast<int64_t>(i1) * p.strides[i][1]
+                       : static_cast<int64_t>(i1) * p.strides[i][0];
+    };
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+      const uint32_t u = base + k * blockDim.x;
+      if (u >= total) break;
 #pragma unroll
       for (int i = 0; i < NIN; ++i) {
-        off[k][i] = RANK == 2 ? static_cast<int64_t>(i0) * p.strides[i][0] + static_cast<int64_t>(i1) * p.strides[i][1]
-                              : static_cast<int64_t>(i1) * p.strides[i][0];
         if (p.inner_stride[i] == 1) {
-          const uint4* q = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.in[i]) + off[k][i] * (2 * W));
+          const uint4* q =
+              reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(p.in[i]) + offset(u, i) * (2 * W));
 #pragma unroll
           for (int w = 0; w < W; ++w) raw[k][i][w] = __ldg(q + w);
         }
       }
     }
     // One copy of the program loop (the interpreter is large): unit k's
-    // operands are always in slot 0 of raw/off, shifted down after each unit.
+    // operands are always in slot 0 of raw, shifted down after each unit.
 #pragma unroll 1
     for (int k = 0; k < U; ++k) {
       const uint32_t u = base + k * blockDim.x;
@@ -175,7 +179,7 @@ __global__ void __launch_bounds__(256) pointwise_fast_kernel(const __grid_consta
             }
           }
         } else {
-          const float sc = load_scalar(p.in[i], off[0][i], p.dt[i]);
+          const float sc = load_scalar(p.in[i], offset(u, i), p.dt[i]);
 #pragma unroll
           for (int j = 0; j < 8; ++j) r[i][j] = sc;
         }
@@ -190,7 +194,6 @@ __global__ void __launch_bounds__(256) pointwise_fast_kernel(const __grid_consta
         for (int i = 0; i < NIN; ++i) {
 #pragma unroll
           for (int w = 0; w < W; ++w) raw[kk][i][w] = raw[kk + 1][i][w];
-          off[kk][i] = off[kk + 1][i];
         }
       }
     }
@@ -201,7 +204,7 @@ namespace {
 
 template <int RANK, int NIN, int W>
 int launch_fast(const PwParams& p, int64_t units, cudaStream_t stream) {
-  constexpr int U = NIN * W <= 1 ? 4 : 2;  // units in flight per thread (more spill past ~128 registers)
+  constexpr int U = NIN * W <= 2 ? 4 : 2;  // units in flight per thread (more spill past ~128 registers)
   auto kernel = pointwise_fast_kernel<RANK, NIN, U, W>;
   const int sms = device_sm_count();
   if (sms <= 0) return B200K_ERR_DEVICE;
