@@ -15,7 +15,7 @@
  * Reference interfaces replaced (aashrith-madasu/torch-compile-backend):
  *   b200k_pointwise      <- the generated `fused_<n>` Triton kernel and its launch
  *                           closure `fused_op(*tensors)`
- *                           compiler/optimization/fusion_pointwise.py:155-192,212-233
+ *                           compiler/optimization/fusion_pointwise.py:132-169,189-210
  *   b200k_gemm_epilogue  <- the generated autotuned `gemm_epilogue_<n>` Triton kernel
  *                           and its closure `epilogue_op(a, b, *tensors)`
  *                           compiler/optimization/fusion_epilogue.py:72-180; also the
@@ -143,6 +143,29 @@ typedef struct {
 } B200kPointwiseArgs;
 
 int b200k_pointwise(const B200kPointwiseArgs* args, void* stream);
+
+/* b200k_pointwise runs a kernel generated for its program (compiled for
+ * sm_100a by NVRTC on first use, cached per process and device) when the
+ * launch merges to rank <= 2 with 32-bit unit indices and every operand is
+ * bf16, f16 or f32 with innermost stride 0 or 1; the reference likewise
+ * compiles one Triton kernel per fused group on first use
+ * (compiler/optimization/fusion_pointwise.py:178-186).  Other launches, and
+ * programs whose kernel could not be compiled or loaded, run the interpreter
+ * kernels.  Setting B200K_POINTWISE_JIT=0 in the environment disables the
+ * generated kernels.
+ *
+ * Counters of this process: kernels compiled and loaded, compile or load
+ * failures, launches of generated kernels.  Any pointer may be null. */
+int b200k_pointwise_jit_stats(int64_t* compiled, int64_t* failed, int64_t* launches);
+
+/* Generates and compiles (no device needed, nothing loaded) the kernel for a
+ * program over `n_inputs` (<= 4) operands of the given dtypes, each with
+ * innermost stride 1 (unit_stride[i] != 0) or 0, at merged rank 1 or 2.
+ * Writes NVRTC's log (truncated, NUL-terminated) to `log` when log_len > 0.
+ * Returns B200K_OK, B200K_ERR_UNSUPPORTED (out of scope) or B200K_ERR_LAUNCH
+ * (NVRTC missing or the compile failed). */
+int b200k_pointwise_jit_compile(int rank, int n_inputs, const int32_t* dtypes, const int32_t* unit_stride,
+                                int32_t out_dtype, const B200kProgram* program, char* log, int64_t log_len);
 
 /* An epilogue operand indexed by the output coordinate (m, n). */
 typedef struct {

@@ -29,7 +29,7 @@ GEMM_TEST_WITHHOLD_READY = 1  # include/b200k.h: failure-detection test hook
 EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
-    "b200k_gemm_epilogue_noalloc", "b200k_rope",
+    "b200k_gemm_epilogue_noalloc", "b200k_rope", "b200k_pointwise_jit_stats", "b200k_pointwise_jit_compile",
 ]
 
 
@@ -119,6 +119,10 @@ def library() -> ctypes.CDLL:
             ("b200k_gemm_config_info", [ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
             ("b200k_gemm_num_configs", []),
             ("b200k_version", []),
+            ("b200k_pointwise_jit_stats", [ctypes.POINTER(ctypes.c_int64)] * 3),
+            ("b200k_pointwise_jit_compile", [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int32),
+                                             ctypes.POINTER(ctypes.c_int32), ctypes.c_int32,
+                                             ctypes.POINTER(Program), ctypes.c_char_p, ctypes.c_int64]),
         ]:
             fn = getattr(lib, name)
             fn.argtypes = argt
@@ -172,6 +176,26 @@ def pointwise(inputs: list[torch.Tensor], code, imm, out: torch.Tensor) -> None:
     a.out_dtype = DTYPE[out.dtype]
     a.program = make_program(code, imm)
     _check("b200k_pointwise", library().b200k_pointwise(ctypes.byref(a), _stream()))
+
+
+def pointwise_jit_stats() -> dict:
+    """This process's generated pointwise kernels: compiled, failed, launches."""
+    v = [ctypes.c_int64() for _ in range(3)]
+    _check("b200k_pointwise_jit_stats", library().b200k_pointwise_jit_stats(*[ctypes.byref(x) for x in v]))
+    return {"compiled": v[0].value, "failed": v[1].value, "launches": v[2].value}
+
+
+def pointwise_jit_compile(rank: int, dtypes: list[int], unit_stride: list[bool], out_dtype: int, code,
+                          imm) -> tuple[int, str]:
+    """Generates and compiles (no GPU needed) the kernel of a program; returns
+    (status code, NVRTC log)."""
+    n = len(dtypes)
+    dt = (ctypes.c_int32 * max(n, 1))(*dtypes)
+    us = (ctypes.c_int32 * max(n, 1))(*[int(bool(u)) for u in unit_stride])
+    prog = make_program(code, imm)
+    log = ctypes.create_string_buffer(8192)
+    rc = library().b200k_pointwise_jit_compile(rank, n, dt, us, out_dtype, ctypes.byref(prog), log, len(log))
+    return rc, log.value.decode(errors="replace")
 
 
 def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], code, imm, out: torch.Tensor,

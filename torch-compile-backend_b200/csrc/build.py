@@ -33,7 +33,7 @@ BUILD_DIR = os.path.join(PKG, "_build")
 # (source, object name, defines).  gemm_fast.cu is compiled once per
 # (tile width, activation) that has compiled-epilogue kernels; the
 # activations are B200K_ACT_NONE, GELU_ERF, GELU_TANH, SILU, RELU.
-CU_UNITS = [(src, os.path.splitext(src)[0], []) for src in ("capi.cu", "pointwise.cu", "rowreduce.cu", "rowreduce16.cu",
+CU_UNITS = [(src, os.path.splitext(src)[0], []) for src in ("capi.cu", "pointwise.cu", "pointwise_jit.cu", "rowreduce.cu", "rowreduce16.cu",
                                                                   "rope.cu", "gemm_sm100.cu")]
 CU_UNITS += [("gemm_fast.cu", f"gemm_fast_{bn}_{act}", [f"-DB200K_FAST_BN={bn}", f"-DB200K_FAST_ACT={act}"])
              for bn in (256, 192, 128) for act in (0, 1, 2, 3, 4)]
@@ -41,7 +41,8 @@ CU_UNITS += [("gemm_fast.cu", f"gemm_fast_{bn}_{act}", [f"-DB200K_FAST_BN={bn}",
 # 4: 256 x 512 tiles)
 CU_UNITS += [("gemm_fast.cu", f"gemm_fast_pair{w}_{act}", [f"-DB200K_FAST_BN={w}", f"-DB200K_FAST_ACT={act}"])
              for w in (2, 4) for act in (0, 1, 2, 3, 4)]
-HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h", "gemm_kernel.cuh", "rowreduce.cuh")] + [
+HEADERS = [os.path.join(HERE, h) for h in ("common.cuh", "host_common.h", "gemm_kernel.cuh", "rowreduce.cuh",
+                                           "pointwise_jit.h")] + [
     os.path.join(INCLUDE, "b200k.h")]
 LIB = os.path.join(OUT_DIR, "libb200k.so")
 EXT = os.path.join(OUT_DIR, "_b200_ops.so")
@@ -98,7 +99,7 @@ def build(force: bool = False, verbose: bool = False) -> tuple[str, str]:
     with cf.ThreadPoolExecutor(max_workers=min(len(CU_UNITS), os.cpu_count() or 4)) as pool:
         objs = list(pool.map(lambda u: _compile_cu(u, force, verbose), CU_UNITS))
         if force or _newer(LIB, objs):
-            _run([NVCC] + ARCH_FLAGS + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs, verbose)
+            _run([NVCC] + ARCH_FLAGS + ["-shared", "-Xcompiler", "-fPIC", "-o", LIB] + objs + ["-ldl"], verbose)
         if force or _newer(EXT, [ext_src, LIB, os.path.join(INCLUDE, "b200k.h")]):
             cflags, ldflags = _torch_flags()
             cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-I" + INCLUDE] + cflags

@@ -1,8 +1,8 @@
 // Fused pointwise chains: out = program(inputs) over a broadcast N-d index space.
 //
 // Replaces the reference's generated elementwise Triton kernel
-// (compiler/optimization/fusion_pointwise.py:155-192) and its launch closure
-// (:224-230).  Where the reference unravels every element's flat index with a
+// (compiler/optimization/fusion_pointwise.py:132-169) and its launch closure
+// (:189-210).  Where the reference unravels every element's flat index with a
 // div/mod per dimension and gathers scalars, this kernel
 //   * coalesces dimensions on the host (adjacent dims that are contiguous for
 //     every operand merge), so most launches are rank 1 or 2;
@@ -16,6 +16,7 @@
 
 #include "common.cuh"
 #include "host_common.h"
+#include "pointwise_jit.h"
 
 namespace b200k {
 
@@ -360,6 +361,23 @@ extern "C" int b200k_pointwise(const B200kPointwiseArgs* a, void* stream_) {
     for (int d = 0; d < nm; ++d) p.div[d] = make_fastdiv(static_cast<uint32_t>(p.sizes[d]));
   }
 
+  // Generated straight-line kernel of this program (pointwise_jit.cu) when
+  // the launch is in its scope; the interpreter kernels below otherwise.
+  if (vec && !i64 && nm <= 2) {
+    PwJitLaunch L;
+    std::memset(&L, 0, sizeof(L));
+    L.rank = nm;
+    L.nin = nin;
+    L.units = units;
+    L.inner_units = nm == 2 ? p.sizes[1] : 0;
+    for (int i = 0; i < nin; ++i) {
+      L.stride0[i] = p.strides[i][0];
+      L.stride1[i] = nm == 2 ? p.strides[i][1] : 0;
+      L.inner_stride[i] = p.inner_stride[i];
+    }
+    const int jrc = pointwise_jit_launch(a, L, stream);
+    if (jrc != B200K_ERR_UNSUPPORTED) return jrc;
+  }
   if (vec && !i64 && nm <= 2 && nin <= 4 && slots_used(a->program, nin) <= kFastSlots) {
     int w = 0;  // 16-byte words per unit, the same for every unit-stride input
     bool fast = true;
