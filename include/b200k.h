@@ -24,7 +24,7 @@
  *   b200k_pointwise (ADD program) <- hand_written/matrix_add_kernel.py:6-46
  *   b200k_rownorm, b200k_softmax  <- no Triton counterpart: the reference leaves
  *                           pow/mean/native_layer_norm/_softmax to ATen
- *                           (compiler/optimization/fusion_pointwise.py:35-53 has no
+ *                           (compiler/optimization/fusion_pointwise.py:12-30 has no
  *                           reduction entries); these fuse the whole row group.
  */
 #ifndef B200K_H
@@ -75,7 +75,7 @@ enum {
  * Instruction word: code = op * 10 + operand, operand 0..7 = slot, 8 = imm,
  * 9 = none.  Binary ops compute acc = acc (op) x; R* ops swap the operands.
  * After the last instruction `acc` is rounded to the output dtype and stored.
- * Op semantics follow compiler/optimization/fusion_pointwise.py:35-53 (fp32
+ * Op semantics follow compiler/optimization/fusion_pointwise.py:12-30 (fp32
  * math; tanh is 2*sigmoid(2x)-1; sigmoid is 1/(1+exp(-x)); relu/max/min return
  * the non-NaN operand).  ROUND_* are for fusions that cross a sub-fp32 cast.
  */
@@ -129,7 +129,7 @@ typedef struct {
 
 /*
  * out[i0..i_{r-1}] = program(inputs at the same index), out contiguous.
- * Replaces fusion_pointwise.py:155-192 (generated kernel) + :224-230 (launch).
+ * Replaces fusion_pointwise.py:132-169 (generated kernel) + :201-207 (launch).
  */
 typedef struct {
   int32_t rank; /* 0..B200K_MAX_DIMS */

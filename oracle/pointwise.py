@@ -1,11 +1,11 @@
 """Oracle for the fused pointwise kernel -- test infrastructure only.
 
 Restates the reference's generated elementwise kernel
-(compiler/optimization/fusion_pointwise.py:155-192): every external input is
+(compiler/optimization/fusion_pointwise.py:132-169): every external input is
 read at the output index through its own broadcast strides and converted to
-fp32 (:185-188), the group's ops run in fp32 one after another with the
-expressions of POINTWISE_OPS (:35-53), Python scalars are fp32 constants
-(:146), and the single store rounds to the output dtype (:191).
+fp32 (:162-165), the group's ops run in fp32 one after another with the
+expressions of POINTWISE_OPS (:12-30), Python scalars are fp32 constants
+(:123), and the single store rounds to the output dtype (:168).
 """
 from __future__ import annotations
 
@@ -23,7 +23,7 @@ def _sigmoid(a):
 
 
 def _tanh(a):
-    # fusion_pointwise.py:49 -- tanh is computed as 2*sigmoid(2x) - 1.
+    # fusion_pointwise.py:26 -- tanh is computed as 2*sigmoid(2x) - 1.
     return (F32(2.0) * _sigmoid(F32(2.0) * a) - F32(1.0)).astype(F32)
 
 

@@ -6,11 +6,11 @@ Run where the reference checkout is available (read-only), not on the GPU box:
 
 Method.  The reference (aashrith-madasu/torch-compile-backend) is imported
 from its checkout with TRITON_INTERPRET=1, so the Triton kernels it generates
-(compiler/optimization/fusion_pointwise.py:155-192,
+(compiler/optimization/fusion_pointwise.py:132-169,
 compiler/optimization/fusion_epilogue.py:72-151) run on CPU through Triton's
 interpreter.  Four things are adjusted so it runs there, none of which
 changes what a kernel computes:
-  * the CUDA-only checks (`val.is_cuda` in _is_fusible, fusion_pointwise.py:93;
+  * the CUDA-only checks (`val.is_cuda` in _is_fusible, fusion_pointwise.py:70;
     _is_static_cuda, fusion_epilogue.py:41-42) accept CPU tensors;
   * the compile-time wall-clock gate (_epilogue_is_faster, :207-234) becomes
     the dtype rule it settles on for B200 (fp32 without TF32 -> cuBLAS, as its

@@ -21,7 +21,7 @@ Environment flags (read once at import, overridable as module attributes):
 
 The reference hard-codes its equivalents (AUTOTUNE_CONFIGS, BLOCK=1024,
 DOT_DTYPES in compiler/optimization/fusion_epilogue.py:23-38 and
-fusion_pointwise.py:229) and has no switches.
+fusion_pointwise.py:206) and has no switches.
 """
 from __future__ import annotations
 
@@ -61,7 +61,7 @@ GEMM_OUT_DTYPES = {torch.float16, torch.bfloat16, torch.float32}
 ROW_DTYPES = {torch.float32, torch.float16, torch.bfloat16}
 
 # The fusions fire only for tensors on this predicate's device: CUDA, as in the
-# reference (fusion_pointwise.py:93, fusion_epilogue.py:41-42).  Tests that
+# reference (fusion_pointwise.py:70, fusion_epilogue.py:41-42).  Tests that
 # inspect the rewritten graph on a CPU-only machine swap it out.
 _device_predicate: Callable[[torch.Tensor], bool] = lambda val: val.is_cuda
 

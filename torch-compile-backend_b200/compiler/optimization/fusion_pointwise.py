@@ -2,13 +2,16 @@
 each group of >= 2 ops with one call of the sm_100a pointwise kernel.
 
 Same public names, grouping rules and argument order as the reference
-(compiler/optimization/fusion_pointwise.py): POINTWISE_OPS (:35-53),
-_is_float_cast / _is_fusible (:67-96), find_fusion_groups (:99-128),
-external_inputs (:131-136), build_fused_op (:212-233), fuse_pointwise
-(:236-254).  What differs is the lowering: instead of writing Triton source to
-a temp file and importing it (:155-209), a group becomes an accumulator-machine
+(compiler/optimization/fusion_pointwise.py): POINTWISE_OPS (:12-30),
+_is_float_cast / _is_fusible (:44-73), find_fusion_groups (:76-105),
+external_inputs (:108-113), build_fused_op (:189-210), fuse_pointwise
+(:213-231).  What differs is the lowering: instead of writing Triton source to
+a temp file and importing it (:132-186), a group becomes an accumulator-machine
 program (optimization/program.py) passed as data to
-``torch.ops.b200.pointwise`` -- one precompiled CUDA kernel for every chain.
+``torch.ops.b200.pointwise``.  The kernel library turns that program into
+straight-line CUDA C and compiles it for sm_100a with NVRTC on first use
+(csrc/pointwise_jit.cu), or interprets it where a launch is outside the
+generated kernels' scope (csrc/pointwise.cu).
 """
 from __future__ import annotations
 

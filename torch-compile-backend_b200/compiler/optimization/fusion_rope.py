@@ -8,7 +8,7 @@ The rotate-half form of RoPE, ``x * cos + rotate_half(x) * sin`` with
       -> mul(x, cos), mul(cat, sin) -> add
 
 The reference's pointwise pass cannot take aten.cat (it is not in
-POINTWISE_OPS, compiler/optimization/fusion_pointwise.py:35-53), so eager
+POINTWISE_OPS, compiler/optimization/fusion_pointwise.py:12-30), so eager
 execution and the reference run neg and cat as separate kernels and the
 fused multiply-add reads the materialised rotation.  This pass replaces the
 whole group with ``torch.ops.b200.rope``, one kernel that reads x, cos and

@@ -1,7 +1,7 @@
 """Row-reduction fusion pass (an extension: the reference has none).
 
-The reference's POINTWISE_OPS (compiler/optimization/fusion_pointwise.py:35-53)
-has no reductions and its groups must share one output shape (:116-120), so
+The reference's POINTWISE_OPS (compiler/optimization/fusion_pointwise.py:12-30)
+has no reductions and its groups must share one output shape (:93-97), so
 RMSNorm, LayerNorm and softmax stay in ATen with only their pointwise
 fragments fused (e.g. RMSNorm -> ATen pow, ATen mean, fused add+rsqrt,
 fused x*r*w).  This pass recognises whole row groups in the decomposed ATen

@@ -1,7 +1,7 @@
 """Lowering of a fused FX group to the kernel library's epilogue program.
 
 The reference turns each group into Triton source, one SSA line per node
-(compiler/optimization/fusion_pointwise.py:139-152, emit_pointwise_ops), and
+(compiler/optimization/fusion_pointwise.py:116-129, emit_pointwise_ops), and
 JIT-compiles it.  Here a group becomes data instead: a short program for the
 accumulator machine that every pointwise and GEMM-epilogue kernel in
 libb200k.so interprets per element (include/b200k.h documents the
@@ -39,7 +39,7 @@ OP_NAME = {v: k for k, v in OP.items()}
 
 # ATen op -> (machine op, swapped-operand machine op or None, is_unary).
 # The set is exactly the reference's POINTWISE_OPS
-# (compiler/optimization/fusion_pointwise.py:35-53); _to_copy is an identity
+# (compiler/optimization/fusion_pointwise.py:12-30); _to_copy is an identity
 # inside a kernel (the final store rounds to the output dtype).
 BINARY = {
     aten.add.Tensor: ("ADD", "ADD"),

@@ -14,7 +14,7 @@ namespace b200k {
 
 // ---------------------------------------------------------------------------
 // Scalar math with the reference's op semantics
-// (compiler/optimization/fusion_pointwise.py:35-53): fp32 everywhere,
+// (compiler/optimization/fusion_pointwise.py:12-30): fp32 everywhere,
 // sigmoid = 1/(1+exp(-x)), tanh = 2*sigmoid(2x)-1, relu/max/min keep the
 // non-NaN operand (Triton's default maximum/minimum).
 // ---------------------------------------------------------------------------

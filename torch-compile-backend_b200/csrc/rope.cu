@@ -2,7 +2,7 @@
 //   out = x * cos + rotate_half(x) * sin.
 //
 // No reference counterpart: the reference's pointwise fusion
-// (compiler/optimization/fusion_pointwise.py:35-53) has no aten.cat, so
+// (compiler/optimization/fusion_pointwise.py:12-30) has no aten.cat, so
 // rotate_half stays two ATen kernels (neg, cat) and the fused x*cos + r*sin
 // reads the materialised rotation.  Here one thread takes 8 consecutive
 // elements of one row of D: its own 16-byte chunk of x and the partner chunk

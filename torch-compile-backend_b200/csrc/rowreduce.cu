@@ -2,7 +2,7 @@
 // softmax / log-softmax over the last dim.
 //
 // No reference counterpart: the reference backend has no reduction entries in
-// POINTWISE_OPS (compiler/optimization/fusion_pointwise.py:35-53) and leaves
+// POINTWISE_OPS (compiler/optimization/fusion_pointwise.py:12-30) and leaves
 // pow/mean/native_layer_norm/_softmax to ATen, fusing only the pointwise
 // fragments between them.  Each kernel here reads its row once from HBM into
 // registers (128-bit loads), reduces with warp shuffles (+ shared memory across

@@ -3,7 +3,7 @@
 //
 // These ops are what the rewritten FX graph calls in place of the reference's
 // Python closures `fused_op(*tensors)` (compiler/optimization/
-// fusion_pointwise.py:224-230) and `epilogue_op(a, b, *tensors)`
+// fusion_pointwise.py:201-207) and `epilogue_op(a, b, *tensors)`
 // (compiler/optimization/fusion_epilogue.py:164-177).  Like those closures they
 // allocate the output with the caching allocator (torch.empty) and launch on
 // the current stream; unlike them they never fall back to anything: a
