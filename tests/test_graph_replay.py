@@ -129,3 +129,105 @@ def test_replay_reads_parameters_in_place():
         want = model(x)
     torch._dynamo.reset()
     torch.testing.assert_close(got.float(), want.float(), rtol=5e-2, atol=5e-2)
+
+
+def _chain_with_head(n_ops: int, big: bool) -> fx.GraphModule:
+    """x -> relu repeated n_ops times -> mm(view(x), t(w)) -> view: the head's
+    output is marked larger than the clone limit when `big`."""
+    g = fx.Graph()
+    x = g.placeholder("x")
+    w = g.placeholder("w")
+    for _ in range(n_ops):
+        x = g.call_function(torch.ops.aten.relu.default, (x,))
+    v = g.call_function(torch.ops.aten.view.default, (x, [-1, 8]))
+    wt = g.call_function(torch.ops.aten.t.default, (w,))
+    mm = g.call_function(torch.ops.aten.mm.default, (v, wt))
+    out = g.call_function(torch.ops.aten.view.default, (mm, [2, -1, 16]))
+    small = g.call_function(torch.ops.aten.neg.default, (x,))
+    n = config.GRAPH_MAX_OUTPUT_MB * 2**20 // 2 + 1 if big else 16
+    out.meta["val"] = torch.empty(n, dtype=torch.bfloat16, device="meta")
+    small.meta["val"] = torch.empty(16, dtype=torch.bfloat16, device="meta")
+    g.output((out, small))
+    return fx.GraphModule(nn.Module(), g)
+
+
+def test_large_outputs_split_into_replayed_body_and_eager_tail():
+    """The head (mm with its views) forms the tail; the relus stay in the
+    replayed body; the tail's inputs are the body's last relu (handed over
+    without a clone) and the weight argument."""
+    gm = _chain_with_head(config.GRAPH_MIN_LAUNCHES, big=True)
+    r = graph_replay.wrap(gm, lambda args: args)
+    assert isinstance(r, graph_replay.TailReplay) and r._boxed_call
+    tail_targets = [n.target for n in r.tail_gm.graph.nodes if n.op == "call_function"]
+    assert sorted(map(str, tail_targets)) == sorted(["aten.view.default", "aten.t.default", "aten.mm.default",
+                                                     "aten.view.default"])
+    assert r.tail_args == [("body", 1), ("arg", 1)]
+    assert r.plan == [("tail", 0), ("body", 0)]
+    assert r.body.no_clone == frozenset({1})
+    # On CPU tensors the body runs op by op; the results equal the graph's.
+    x, w = torch.randn(4, 8), torch.randn(16, 8)
+    got = r([x, w])
+    want = gm(x, w)
+    assert len(got) == 2 and all(torch.equal(a, b) for a, b in zip(got, want))
+
+
+def test_small_outputs_replay_whole_and_unsplittable_graphs_run_op_by_op():
+    gm = _chain_with_head(config.GRAPH_MIN_LAUNCHES, big=False)
+    assert isinstance(graph_replay.wrap(gm, lambda a: a), graph_replay.GraphReplay)
+    # too few launches left in the body once the head is split off
+    gm = _chain_with_head(config.GRAPH_MIN_LAUNCHES - 2, big=True)
+    fn = lambda a: a  # noqa: E731
+    assert graph_replay.wrap(gm, fn) is fn
+    # the head's input also feeds another output: the tail would be read by the body
+    gm = _chain_with_head(config.GRAPH_MIN_LAUNCHES, big=True)
+    mm = next(n for n in gm.graph.nodes if n.target == torch.ops.aten.mm.default)
+    out = next(n for n in gm.graph.nodes if n.op == "output")
+    with gm.graph.inserting_before(out):
+        extra = gm.graph.call_function(torch.ops.aten.relu.default, (mm,))
+    out.args = ((out.args[0][0], out.args[0][1], extra),)
+    gm.recompile()
+    assert graph_replay.wrap(gm, fn) is fn
+
+
+class _BlocksWithHead(_Blocks):
+    def __init__(self, dim=256, depth=6, vocab=4096):
+        super().__init__(dim, depth)
+        self.head = nn.Linear(dim, vocab, bias=False)
+
+    def forward(self, x):
+        return self.head(super().forward(x))
+
+
+@pytest.mark.gpu
+def test_split_replay_matches_op_by_op_and_outputs_survive_later_calls(monkeypatch):
+    """A model whose output is above the clone limit (lowered to 1 MiB here):
+    the body replays, the head runs op by op into fresh tensors, results equal
+    the op-by-op compiled function's bit for bit and stay valid after later
+    calls."""
+    from compiler.backend import custom_backend
+
+    monkeypatch.setattr(config, "GRAPH_MAX_OUTPUT_MB", 1)
+    torch.manual_seed(2)
+    model = _BlocksWithHead().to(DEV, torch.bfloat16).eval()
+    xs = [torch.randn(512, 256, device=DEV, dtype=torch.bfloat16) for _ in range(4)]
+    torch._dynamo.reset()
+    before = graph_replay.REPLAYS
+    with torch.no_grad():
+        f = torch.compile(model, backend=custom_backend)
+        outs = [f(x) for x in xs]
+        kept = [o.clone() for o in outs]
+        f(torch.randn(512, 256, device=DEV, dtype=torch.bfloat16))
+    torch.cuda.synchronize()
+    assert graph_replay.REPLAYS - before >= 3
+    assert all(o.shape == (512, 4096) for o in outs)
+    assert len({o.data_ptr() for o in outs}) == len(outs)  # fresh output tensors
+    for o, k in zip(outs, kept):
+        assert torch.equal(o, k)
+    monkeypatch.setattr(config, "CUDA_GRAPHS", False)
+    torch._dynamo.reset()
+    with torch.no_grad():
+        g = torch.compile(model, backend=custom_backend)
+        want = [g(x) for x in xs]
+    torch._dynamo.reset()
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)

@@ -22,11 +22,17 @@ The graph's intermediate buffers stay allocated (in a private memory pool)
 for the life of the compiled function.  Only inference graphs with at least
 ``config.GRAPH_MIN_LAUNCHES`` launching nodes and CUDA inputs take this path;
 training graphs, whose forward outputs are saved for the backward pass, do
-not.  A graph whose outputs exceed ``config.GRAPH_MAX_OUTPUT_MB`` runs op by
-op: cloning them costs more than replay saves (measured on B200: ViT-B/16,
+not.  Outputs above ``config.GRAPH_MAX_OUTPUT_MB`` are not cloned out of a
+graph: cloning them costs more than replay saves (measured on B200: ViT-B/16,
 90 launches and a [64, 1000] output, 3.142 -> 2.998 ms per forward; the
 Llama-style prefill, 195 launches of mostly long GEMMs and a 4.2 GB logits
-output, 37.17 -> 38.36 ms).
+output, 37.17 -> 38.36 ms with the logits cloned).  Such a graph is split
+(``split_large_outputs``): the launching nodes that produce the large outputs,
+with the views around them, form a tail that runs op by op into fresh
+tensors, and the rest of the graph -- the body -- is replayed.  The body's
+values that only the tail reads are handed over without a copy: the tail's
+launches follow the replay on the same stream, before any later replay can
+overwrite them.
 """
 from __future__ import annotations
 
@@ -71,8 +77,9 @@ class GraphReplay:
 
     _boxed_call = True  # AOTAutograd's marker for the list-argument calling convention
 
-    def __init__(self, fn):
+    def __init__(self, fn, no_clone=()):
         self.fn = fn  # boxed op-by-op function of the compiled graph
+        self.no_clone = frozenset(no_clone)  # output indices returned as the graph's own buffers
         self.calls = 0
         self.replays = 0
         self.graph = None
@@ -114,7 +121,8 @@ class GraphReplay:
         storages = {a.untyped_storage().data_ptr() for a in self.static_in if isinstance(a, torch.Tensor)}
         if any(isinstance(o, torch.Tensor) and o.untyped_storage().data_ptr() in storages for o in outs):
             raise RuntimeError("an output aliases an input")
-        out_bytes = sum(o.numel() * o.element_size() for o in outs if isinstance(o, torch.Tensor))
+        out_bytes = sum(o.numel() * o.element_size() for i, o in enumerate(outs)
+                        if isinstance(o, torch.Tensor) and i not in self.no_clone)
         if out_bytes > config.GRAPH_MAX_OUTPUT_MB * 2**20:
             raise RuntimeError("outputs too large to clone per call")
         self.graph, self.static_out = graph, outs
@@ -146,7 +154,8 @@ class GraphReplay:
         self.replays += 1
         global REPLAYS
         REPLAYS += 1
-        return [o.clone() if isinstance(o, torch.Tensor) else o for o in self.static_out]
+        return [o.clone() if isinstance(o, torch.Tensor) and i not in self.no_clone else o
+                for i, o in enumerate(self.static_out)]
 
 
 def output_bytes(gm: fx.GraphModule) -> int:
@@ -163,11 +172,129 @@ def output_bytes(gm: fx.GraphModule) -> int:
     return total
 
 
+def _node_bytes(n) -> int:
+    v = n.meta.get("val") if isinstance(n, fx.Node) else None
+    return v.numel() * v.element_size() if isinstance(v, torch.Tensor) else 0
+
+
+def _launches(n: fx.Node) -> bool:
+    return (n.op == "call_function" and n.target not in _NO_LAUNCH
+            and getattr(n.target, "__name__", "") != "getitem")
+
+
+class TailReplay:
+    """Boxed callable of a split graph: the body replayed (GraphReplay), then
+    the tail op by op on the body's values and the graph's inputs."""
+
+    _boxed_call = True
+
+    def __init__(self, body: GraphReplay, tail_gm: fx.GraphModule, n_body_outs: int, plan, tail_args):
+        self.body = body
+        self.tail_gm = tail_gm
+        self.n_body_outs = n_body_outs  # body outputs that are graph outputs
+        self.plan = plan  # per graph output: ("body", i), ("tail", i) or ("const", value)
+        self.tail_args = tail_args  # per tail input: ("body", i) or ("arg", i)
+
+    def __call__(self, args):
+        b = self.body(args)
+        t_in = [b[i] if kind == "body" else args[i] for kind, i in self.tail_args]
+        t = self.tail_gm(*t_in)
+        out = []
+        for kind, v in self.plan:
+            out.append(b[v] if kind == "body" else t[v] if kind == "tail" else v)
+        return out
+
+
+def split_large_outputs(gm: fx.GraphModule):
+    """A TailReplay of `gm` whose tail computes the outputs larger than
+    ``config.GRAPH_MAX_OUTPUT_MB``, or None when the graph does not split
+    cleanly (a large output that is an input, a tail value that the body also
+    reads, or too few launches left in the body)."""
+    limit = config.GRAPH_MAX_OUTPUT_MB * 2**20
+    out_node = next(n for n in gm.graph.nodes if n.op == "output")
+    outs = out_node.args[0]
+    outs = list(outs) if isinstance(outs, (list, tuple)) else [outs]
+    big = [o for o in outs if isinstance(o, fx.Node) and _node_bytes(o) > limit]
+    if not big or any(o.op != "call_function" for o in big):
+        return None
+    # The tail: each large output's producer chain back to (and including) its
+    # first launching node, plus every view feeding a tail node.
+    tail, stack = set(), [(o, False) for o in big]
+    while stack:
+        n, past_launch = stack.pop()
+        if n in tail or n.op != "call_function":
+            continue
+        if past_launch and _launches(n):
+            continue  # a launching input of the producer stays in the body
+        tail.add(n)
+        for a in n.all_input_nodes:
+            stack.append((a, past_launch or _launches(n)))
+    for n in tail:
+        if any(u not in tail and u is not out_node for u in n.users):
+            return None
+    if not any(_launches(n) for n in tail):
+        return None
+    order = [n for n in gm.graph.nodes if n in tail]
+    ext = []
+    for n in order:
+        for a in n.all_input_nodes:
+            if a not in tail and a not in ext:
+                ext.append(a)
+
+    # Body: every node outside the tail; outputs = the graph's other outputs,
+    # then the tail's inputs that the body computes.
+    body_g = fx.Graph()
+    env = {}
+    placeholders = []
+    for n in gm.graph.nodes:
+        if n.op == "output" or n in tail:
+            continue
+        env[n] = body_g.node_copy(n, lambda a: env[a])
+        if n.op == "placeholder":
+            placeholders.append(n)
+    small = [o for o in outs if isinstance(o, fx.Node) and o not in tail]
+    ext_body = [a for a in ext if a.op != "placeholder"]
+    if any(o.op == "placeholder" for o in small):
+        return None  # an input returned as an output: the replay would alias it
+    body_g.output(tuple(env[o] for o in small) + tuple(env[a] for a in ext_body))
+    body_gm = fx.GraphModule(gm, body_g)
+    if launching_nodes(body_gm) < config.GRAPH_MIN_LAUNCHES:
+        return None
+
+    # Tail: placeholders for its inputs, then its nodes in graph order.
+    tail_g = fx.Graph()
+    tenv = {a: tail_g.placeholder(f"t_in{i}") for i, a in enumerate(ext)}
+    for a, ph in tenv.items():
+        ph.meta = dict(a.meta)
+    for n in order:
+        tenv[n] = tail_g.node_copy(n, lambda a: tenv[a])
+    tail_outs = [o for o in outs if isinstance(o, fx.Node) and o in tail]
+    tail_g.output(tuple(tenv[o] for o in tail_outs))
+    tail_gm = fx.GraphModule(gm, tail_g)
+
+    plan = []
+    for o in outs:
+        if isinstance(o, fx.Node) and o in tail:
+            plan.append(("tail", tail_outs.index(o)))
+        elif isinstance(o, fx.Node):
+            plan.append(("body", small.index(o)))
+        else:
+            plan.append(("const", o))
+    tail_args = [("arg", placeholders.index(a)) if a.op == "placeholder" else ("body", len(small) + ext_body.index(a))
+                 for a in ext]
+    no_clone = range(len(small), len(small) + len(ext_body))
+    body = GraphReplay(lambda a: body_gm(*a), no_clone=no_clone)
+    return TailReplay(body, tail_gm, len(small), plan, tail_args)
+
+
 def wrap(gm: fx.GraphModule, boxed_fn):
     """The boxed function of an inference graph, replayed as a CUDA graph when
-    it launches enough kernels to gain from it and its outputs are small
-    enough to clone per call; otherwise `boxed_fn`."""
-    if (not config.CUDA_GRAPHS or launching_nodes(gm) < config.GRAPH_MIN_LAUNCHES
-            or output_bytes(gm) > config.GRAPH_MAX_OUTPUT_MB * 2**20):
+    it launches enough kernels to gain from it: whole when its outputs are
+    small enough to clone per call, else split into a replayed body and a
+    tail run op by op (``split_large_outputs``); otherwise `boxed_fn`."""
+    if not config.CUDA_GRAPHS or launching_nodes(gm) < config.GRAPH_MIN_LAUNCHES:
         return boxed_fn
-    return GraphReplay(boxed_fn)
+    if output_bytes(gm) <= config.GRAPH_MAX_OUTPUT_MB * 2**20:
+        return GraphReplay(boxed_fn)
+    split = split_large_outputs(gm)
+    return split if split is not None else boxed_fn
