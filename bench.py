@@ -10,7 +10,8 @@ of the library's tcgen05 GEMM kernel with the epilogue fused.  `value` is the
 sweep's total FLOPs (2MNK per GEMM) / device time, inputs resident in HBM.
 `e2e` is the same metric through the public API (torch.compile with
 custom_backend) with X and R copied in from pinned host memory and Y copied
-back inside the timed region.
+back inside the timed region; the copies run on two copy streams, so one
+GEMM's transfers overlap its neighbours' compute.
 
 Multi-GPU: one process per GPU (torchrun), each GPU runs the full sweep as an
 independent replica (weak scaling, no data-path collective); a gloo process
@@ -310,22 +311,40 @@ def run_sweep(args, dist: Dist) -> dict:
     h2d = sum(hx.numel() * 2 + hr.numel() * 2 for hx, hr, _ in host)
     d2h = sum(hy.numel() * 2 for _, _, hy in host)
 
+    # The copies run on their own streams, so the PCIe transfers of one GEMM
+    # overlap the compute of its neighbours (as a serving loop would run it):
+    # host->device on `up`, the compiled call on the current stream, the
+    # result's device->host on `down`.  record_stream keeps the caching
+    # allocator from reusing a buffer before the stream that reads it is done.
+    compute = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+
     def e2e_step():
         for (hx, hr, hy), f in zip(host, compiled):
-            x = hx.to(dev, non_blocking=True)
-            r = hr.to(dev, non_blocking=True)
+            with torch.cuda.stream(up):
+                x = hx.to(dev, non_blocking=True)
+                r = hr.to(dev, non_blocking=True)
+            compute.wait_stream(up)
+            x.record_stream(compute)
+            r.record_stream(compute)
             with torch.no_grad():
                 y = f(x, r)
-            hy.copy_(y, non_blocking=True)
+            down.wait_stream(compute)
+            with torch.cuda.stream(down):
+                hy.copy_(y, non_blocking=True)
+            y.record_stream(down)
 
     for _ in range(max(1, args.warmup)):
         e2e_step()
+    compute.wait_stream(down)
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
+    up.wait_stream(compute)  # no copy starts before e0
     for _ in range(args.steps):
         e2e_step()
+    compute.wait_stream(down)  # e1 follows the last result's copy to the host
     e1.record()
     torch.cuda.synchronize()
     dist.barrier()
