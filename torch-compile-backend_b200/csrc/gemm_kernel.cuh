@@ -451,32 +451,69 @@ __device__ __forceinline__ float approx_exp2(float x) {
 // 2^(-x^2 log2(e) / 2).  Absolute error of the result is below
 // 1e-7 (1 + |x|) plus the hardware rcp/ex2 rounding; +inf maps to +inf and
 // NaN / -inf to NaN as in the erf formula.  Written stage by stage over the
-// eight values so the independent chains interleave.
+// eight values so the independent chains interleave, two values per
+// instruction with the sm_100 packed fp32 ops (__ffma2_rn, __fmul2_rn: each
+// lane rounds exactly as fmaf / __fmul_rn does).  The polynomial runs on the
+// negated coefficients, which gives -q and then -(q t) bit for bit (round to
+// nearest is symmetric in sign), so r = fma(-(q t), e, 1/2) needs no
+// separate negation.
+__device__ __forceinline__ float2 splat2(float a) { return make_float2(a, a); }
+
 __device__ __forceinline__ void gelu_erf_as8(float (&v)[8]) {
-  float t[8], e[8];
+  float2 x[4], ax[4], t[4], e[4];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) t[j] = approx_rcp(fmaf(0.2316418882663604f, fabsf(v[j]), 1.0f));
+  for (int i = 0; i < 4; ++i) {
+    x[i] = make_float2(v[2 * i], v[2 * i + 1]);
+    ax[i] = make_float2(fabsf(v[2 * i]), fabsf(v[2 * i + 1]));
+  }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) e[j] = approx_exp2((v[j] * -0.72134752044448170f) * v[j]);
+  for (int i = 0; i < 4; ++i) {
+    const float2 a = __ffma2_rn(splat2(0.2316418882663604f), ax[i], splat2(1.0f));
+    t[i] = make_float2(approx_rcp(a.x), approx_rcp(a.y));
+  }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    float q = fmaf(0.5307027145f, t[j], -0.7265760135f);
-    q = fmaf(q, t[j], 0.7107068705f);
-    q = fmaf(q, t[j], -0.142248368f);
-    q = fmaf(q, t[j], 0.127414796f);
-    const float r = fmaf(-(q * t[j]), e[j], 0.5f);
-    v[j] = fmaf(fabsf(v[j]), r, 0.5f * v[j]);
+  for (int i = 0; i < 4; ++i) {
+    const float2 b = __fmul2_rn(__fmul2_rn(x[i], splat2(-0.72134752044448170f)), x[i]);
+    e[i] = make_float2(approx_exp2(b.x), approx_exp2(b.y));
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 nq = __ffma2_rn(splat2(-0.5307027145f), t[i], splat2(0.7265760135f));
+    nq = __ffma2_rn(nq, t[i], splat2(-0.7107068705f));
+    nq = __ffma2_rn(nq, t[i], splat2(0.142248368f));
+    nq = __ffma2_rn(nq, t[i], splat2(-0.127414796f));
+    const float2 r = __ffma2_rn(__fmul2_rn(nq, t[i]), e[i], splat2(0.5f));
+    const float2 o = __ffma2_rn(ax[i], r, __fmul2_rn(splat2(0.5f), x[i]));
+    v[2 * i] = o.x;
+    v[2 * i + 1] = o.y;
+  }
+}
+
+// v[j] = v[j] + b[j] (or * b[j]) for j < 2 N, each rounded once, two per
+// instruction.
+template <int N2, bool MUL>
+__device__ __forceinline__ void op2_rn(float* v, const float* b) {
+#pragma unroll
+  for (int j = 0; j < N2; ++j) {
+    const float2 a = make_float2(v[2 * j], v[2 * j + 1]), c = make_float2(b[2 * j], b[2 * j + 1]);
+    const float2 d = MUL ? __fmul2_rn(a, c) : __fadd2_rn(a, c);
+    v[2 * j] = d.x;
+    v[2 * j + 1] = d.y;
   }
 }
 
 // Separate ops of the decomposed graph (bias add, the activation's final
-// multiply, the scale / residual op) use __fadd_rn / __fmul_rn so the compiler
-// never contracts two of them into one rounding, as eager execution would not.
+// multiply, the scale / residual op) use __fadd_rn / __fmul_rn or their packed
+// forms (op2_rn) so the compiler never contracts two of them into one
+// rounding, as eager execution would not.
 template <int ACT>
 __device__ __forceinline__ void apply_act8(float (&v)[8]) {
   if constexpr (ACT == B200K_ACT_GELU_ERF) {
     gelu_erf_as8(v);
   } else {
+  float x0[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) x0[j] = v[j];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
     const float x = v[j];
@@ -484,7 +521,7 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
       const float t3 = x + ((x * x) * x) * 0.044715f;
       v[j] = (x * 0.5f) * (op_tanh(t3 * 0.7978845608028654f) + 1.0f);
     } else if constexpr (ACT == B200K_ACT_SILU) {
-      v[j] = __fmul_rn(x, op_sigmoid(x));
+      v[j] = op_sigmoid(x);  // times x below, two per instruction
     } else if constexpr (ACT == B200K_ACT_RELU) {
       v[j] = fmaxf(x, 0.0f);
     } else if constexpr (ACT == B200K_ACT_SIGMOID) {
@@ -493,6 +530,7 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
       v[j] = op_tanh(x);
     }
   }
+  if constexpr (ACT == B200K_ACT_SILU) op2_rn<4, true>(v, x0);
   }
 }
 
@@ -569,11 +607,9 @@ __device__ __forceinline__ void add_bias32(const Params& p, int n, float (&v)[32
     const float4* q = reinterpret_cast<const float4*>(p.bias_ptr) + (n >> 2);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float4 b = __ldg(q + i);
-      v[4 * i] = __fadd_rn(v[4 * i], b.x);
-      v[4 * i + 1] = __fadd_rn(v[4 * i + 1], b.y);
-      v[4 * i + 2] = __fadd_rn(v[4 * i + 2], b.z);
-      v[4 * i + 3] = __fadd_rn(v[4 * i + 3], b.w);
+      const float4 b4 = __ldg(q + i);
+      const float b[4] = {b4.x, b4.y, b4.z, b4.w};
+      op2_rn<2, false>(&v[4 * i], b);
     }
     return;
   }
@@ -604,8 +640,7 @@ __device__ __forceinline__ void add_bias32(const Params& p, int n, float (&v)[32
       }
     }
   }
-#pragma unroll
-  for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], b[j]);
+  op2_rn<16, false>(v, b);
 }
 
 // Eight 16-bit values of one row from column n, zero at and beyond column N.
@@ -753,8 +788,7 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
       for (int g = 0; g < 4; ++g) {
         float x[8];
         unpack16x8(use.row_r[g], out_bf16 ? B200K_BF16 : B200K_F16, x);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) v[8 * g + j] = kMul ? __fmul_rn(v[8 * g + j], x[j]) : __fadd_rn(v[8 * g + j], x[j]);
+        op2_rn<4, kMul>(&v[8 * g], x);
       }
     }
     if constexpr (OUT_BYTES == 2) {
