@@ -56,7 +56,8 @@ def test_tile_config_pick_rules():
                     (1, 8, 8), (16384, 4096, 1535)]:
         c = lib.b200k_gemm_pick_config(M, N, K)
         assert 0 <= c < n and info[c][0] == 128, (M, N, K, c)
-    for M, N, K in [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 2048, 2048)]:
+    for M, N, K in [(4096, 4096, 4096), (8192, 8192, 8192), (16384, 2048, 2048), (16384, 8192, 2048),
+                    (16384, 2048, 8192), (12608, 768, 3072)]:
         c = lib.b200k_gemm_pick_config(M, N, K)
         assert info[c] == (256, 256), (M, N, K, c)
     assert info[lib.b200k_gemm_pick_config(16384, 4096, 14336)] == (256, 512)

@@ -96,6 +96,11 @@ int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) 
   // from K = 2048 up (4096^3 1148 -> 1321 TFLOP/s, 16384 x 4096 x 14336 with
   // GELU 1342 -> 1502), no faster at K = 768, where the epilogue bounds a tile
   // and the 192-wide tile's twelve epilogue warps win; pairs need K >= 1536.
+  // From K = 1536 the 192-wide tile is costed at 1.25 per column: there the
+  // main loop, not the epilogue, bounds a tile, and its 128 x 192 share moves
+  // more operand bytes per FLOP than a pair's.  Measured on B200 at 12608 x
+  // 768 x 3072 (bias + residual), both in 3 waves: 128 x 192 tiles 72.7 us
+  // (62 % of the per-SM MMA rate), 256 x 256 pair tiles 67.6 us (88 %).
   // The 256 x 512 pair tile moves 3/4 of the operand bytes per FLOP of the
   // 256 x 256 one, but its single accumulator makes each tile's MMAs wait
   // for the previous tile's epilogue (~10-20 us): measured on B200, 16384 x
@@ -112,7 +117,7 @@ int pick(int64_t M, int64_t N, int64_t K, int sms, bool compiled, bool pair_ok) 
     const int64_t tiles = ((M + bm - 1) / bm) * ((N + bn - 1) / bn);
     const int64_t slots = pair ? sms / 2 : sms;  // tiles that run at once
     const int64_t waves = (tiles + slots - 1) / slots;
-    const double per_col = wide ? 0.82 : pair ? 0.9 : (bn == 256 ? 1.0 : (bn == 192 ? 1.05 : 1.5));
+    const double per_col = wide ? 0.82 : pair ? 0.9 : (bn == 256 ? 1.0 : (bn == 192 ? (K >= 1536 ? 1.25 : 1.05) : 1.5));
     const double cost = static_cast<double>(waves) * bn * per_col;
     if (cost < best_cost) {
       best_cost = cost;
