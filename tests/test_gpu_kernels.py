@@ -418,9 +418,12 @@ def test_rms_norm(dtype, cols):
     _assert_close(out, want, *tol)
 
 
-@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (10, 1024), (3, 50), (5, 16384), (7, 1536), (9, 3072)])
+@pytest.mark.parametrize("rows,cols", [(64 * 197, 768), (64 * 197 + 1, 768), (10, 1024), (3, 50), (17, 520),
+                                       (1, 768), (5, 16384), (7, 1536), (9, 3072)])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 def test_layer_norm(rows, cols, dtype):
+    """Full-size, odd and ragged row counts; the check covers the first and
+    the last rows."""
     dt = _tdt(dtype)
     x = torch.randn(rows, cols, device=DEV).to(dt)
     w = torch.randn(cols, device=DEV).to(dt)
@@ -430,12 +433,12 @@ def test_layer_norm(rows, cols, dtype):
     rstd = torch.empty(rows, device=DEV)
     cabi.rownorm(x, cabi.ROW_LAYERNORM, w, b, 1e-6, 0, out, mean_out=mean, rstd_out=rstd)
     torch.cuda.synchronize()
-    sel = slice(0, 500)
-    o, m, r = oracle.layer_norm(x[sel].float().cpu().numpy(), w.float().cpu().numpy(), b.float().cpu().numpy(), 1e-6,
-                                dtype)
-    _assert_close(out[sel], o, 1e-2, 2e-2)
-    _assert_close(mean[sel], m[:, 0], 1e-5, 1e-5)
-    _assert_close(rstd[sel], r[:, 0], 1e-4, 1e-5)
+    for sel in (slice(0, 500), slice(max(0, rows - 300), rows)):
+        o, m, r = oracle.layer_norm(x[sel].float().cpu().numpy(), w.float().cpu().numpy(),
+                                    b.float().cpu().numpy(), 1e-6, dtype)
+        _assert_close(out[sel], o, 1e-2, 2e-2)
+        _assert_close(mean[sel], m[:, 0], 1e-5, 1e-5)
+        _assert_close(rstd[sel], r[:, 0], 1e-4, 1e-5)
 
 
 @pytest.mark.parametrize("rows,cols", [(32768, 4096), (7, 1000), (3, 33), (2, 32768), (6, 8192), (5, 2048),
