@@ -301,7 +301,13 @@ def run_sweep(args, dist: Dist) -> dict:
     err = ((y[:8].float() - ref).abs().max() / ref.abs().max()).item()
 
     # End to end through torch.compile(custom_backend) with host buffers.
+    # The twelve blocks are instances of one class, so dynamo compiles the
+    # same frame once per block: its recompile limit (8 by default) would
+    # send the last blocks to eager PyTorch.  Raise it for this run and make
+    # hitting it an error, so every e2e call goes through the backend.
     torch._dynamo.reset()
+    torch._dynamo.config.recompile_limit = max(torch._dynamo.config.recompile_limit, 4 * len(probs))
+    torch._dynamo.config.fail_on_recompile_limit_hit = True
     compiled = [torch.compile(p["block"], backend=custom_backend) for p in probs]
     host = []
     for p in probs:
@@ -334,9 +340,15 @@ def run_sweep(args, dist: Dist) -> dict:
                 hy.copy_(y, non_blocking=True)
             y.record_stream(down)
 
+    from compiler import backend as _backend
+
+    graphs0 = _backend.GRAPHS_COMPILED
     for _ in range(max(1, args.warmup)):
         e2e_step()
     compute.wait_stream(down)
+    e2e_graphs = _backend.GRAPHS_COMPILED - graphs0
+    if e2e_graphs < len(probs):
+        raise RuntimeError(f"only {e2e_graphs} of {len(probs)} e2e blocks compiled through the backend")
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -387,7 +399,8 @@ def run_sweep(args, dist: Dist) -> dict:
                      "kernel": _dominant_kernel()[0] + " 16384x4096x14336 gelu",
                      "traffic": profile_traffic(_dominant_kernel()[1]) if _dominant_kernel()[1] else None},
         "e2e": {"value": round(n * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
-                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3)},
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
+                "graphs_compiled": e2e_graphs},
         "gpu_launches": args.steps * len(probs),
         "clocks": clk.summary(),
         "sweep": sweep_detail,

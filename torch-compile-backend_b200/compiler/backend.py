@@ -38,7 +38,14 @@ def _dump(gm: fx.GraphModule) -> None:
                 print(f"#   program: {n.meta['b200_program']}")
 
 
+# Graphs this process has compiled through the backend (a diagnostic count:
+# callers check that their calls really went through it).
+GRAPHS_COMPILED = 0
+
+
 def _passes(gm: fx.GraphModule) -> fx.GraphModule:
+    global GRAPHS_COMPILED
+    GRAPHS_COMPILED += 1
     if config.EXTENSIONS and config.ENABLE_PATCHIFY:
         gm = fuse_patchify(gm)  # patch-embedding convolutions -> im2col + addmm (extension)
     if config.EXTENSIONS:
