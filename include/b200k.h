@@ -265,13 +265,22 @@ int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
  * before the launch); a larger need is rejected with B200K_ERR_SHAPE.
  * The first call on a device looks up that device's copy of the array
  * (cudaGetSymbolAddress, with the device current); make that first call
- * before any stream capture.  All calls share the array: calls whose kernels
- * overlap on the GPU race on the status word.  Inputs and outputs are passed
- * as for b200k_gemm_epilogue; nothing is allocated or freed.
+ * before any stream capture: a first call on a capturing stream returns
+ * B200K_ERR_LAUNCH and enqueues nothing.  The looked-up address is kept for
+ * the life of the process; cudaDeviceReset invalidates it.  All calls share
+ * the array: calls whose kernels overlap on the GPU race on the status word.
+ * Inputs and outputs are passed as for b200k_gemm_epilogue; nothing is
+ * allocated or freed.
  */
 #define B200K_NOALLOC_SCRATCH_BYTES 256
 #define B200K_NOALLOC_STATUS_BYTES 4
 int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream);
+/* Reads the status word of the last b200k_gemm_epilogue_noalloc call on this
+ * device into *host_out (B200K_OK, or B200K_ERR_TIMEOUT when one of its
+ * device-side waits ran out): copies it on `stream` and synchronises with
+ * that stream, so call it after the GEMM's launch on the same stream.  No
+ * reference counterpart; allocates nothing (host_out is caller memory). */
+int b200k_gemm_noalloc_status(int32_t* host_out, void* stream);
 
 /* Number of GEMM tile configurations in the built-in table and their shapes
  * (block_m x block_n).  Config 2 (128 x 192 tiles) runs compiled epilogues

@@ -2,7 +2,7 @@
 
 Run where the reference checkout is available (read-only), not on the GPU box:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of the reference>
 
 Method.  The reference (aashrith-madasu/torch-compile-backend) is imported
 from its checkout with TRITON_INTERPRET=1, so the Triton kernels it generates
@@ -65,7 +65,9 @@ def _spec(group, operand_index, acc_node=None):
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("B200_REFERENCE_DIR"),
+                    required="B200_REFERENCE_DIR" not in os.environ,
+                    help="checkout of the reference repository (or set B200_REFERENCE_DIR)")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from compiler import backend as rb  # the reference's package

@@ -7,6 +7,7 @@ import torch.nn.functional as F
 
 import bench_models as bm
 from cases import CASES, make_case
+from compiler import runtime
 from compiler.backend import backend, custom_backend
 from helpers import b200_targets, capturing_backend
 
@@ -66,6 +67,7 @@ def test_vit_block_stack_bf16():
     # proj+res, fc1+gelu, fc2+res per block; qkv (bias only, no pointwise tail) stays cuBLAS
     assert t.count("b200.gemm_epilogue.default") == 3 * 2
     assert "b200.layer_norm.default" in t
+    runtime.check_status()
     ops = [n.target for g in graphs for n in g.graph.nodes if n.op == "call_function"]
     assert torch.ops.aten.convolution.default not in ops  # patch embedding lowered to a GEMM
     assert _rel(got, want) < 2e-2
@@ -89,6 +91,7 @@ def test_llama_small_bf16():
     epi = [n for g in graphs for n in g.graph.nodes if n.op == "call_function"
            and n.target == torch.ops.b200.gemm_epilogue.default]
     assert len(epi) == 3 * 2 and all(list(n.args[7]) for n in epi)
+    runtime.check_status()
     assert _rel(got, want) < 2e-2
 
 
@@ -134,3 +137,48 @@ def test_hand_written_api():
         matrix_add(a, b.half())
     with pytest.raises(ValueError):
         matrix_add(a.int(), b.int())
+
+
+def test_gemm_timeout_surfaces_through_compiled_graph():
+    """A fused GEMM whose device-side wait runs out (the test hook withholds
+    its first tile's accumulator-ready signal for one launch) is reported by
+    the compiled graph's next call as a RuntimeError; the error is reported
+    once and later calls compute the right result again."""
+    class Block(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.fc = torch.nn.Linear(512, 512)
+
+        def forward(self, x):
+            return F.gelu(self.fc(x)) + x
+
+    torch.manual_seed(0)
+    m = Block().to(DEV, torch.bfloat16).eval()
+    x = torch.randn(256, 512, device=DEV, dtype=torch.bfloat16)
+    torch._dynamo.reset()
+    runtime.check_status()
+    f = torch.compile(m, backend=custom_backend)
+    with torch.no_grad():
+        want = f(x).clone()
+        torch.ops.b200.gemm_test_stall_next(50_000_000)
+        f(x)
+        torch.cuda.synchronize()
+        with pytest.raises(RuntimeError, match="timed out"):
+            f(x)
+        got = f(x)
+        runtime.check_status()
+    assert torch.equal(got, want)
+
+
+def test_check_status_raises_after_a_stalled_gemm():
+    a = torch.randn(256, 512, device=DEV, dtype=torch.bfloat16)
+    w = torch.randn(512, 512, device=DEV, dtype=torch.bfloat16)
+    runtime.check_status()
+    from compiler.optimization.program import OP
+
+    torch.ops.b200.gemm_test_stall_next(50_000_000)
+    torch.ops.b200.gemm_epilogue(a, w.t(), [], [OP["MOV"] * 10], [0.0], [256, 512], torch.bfloat16,
+                                 [1, -1, 0, -1, -1, -1])
+    with pytest.raises(RuntimeError, match="status 6"):
+        runtime.check_status()
+    runtime.check_status()  # cleared

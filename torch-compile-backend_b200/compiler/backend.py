@@ -65,9 +65,50 @@ def _passes(gm: fx.GraphModule) -> fx.GraphModule:
     return gm
 
 
+class StatusChecked:
+    """Boxed callable around a compiled graph that launches GEMMs: before each
+    call it raises if an earlier GEMM on the device reported a device-side
+    timeout, and after the call it queues an asynchronous read-back of the
+    device's status word (``torch.ops.b200.status_check``).  Without it a
+    timed-out GEMM would hand a partly written tensor to the rest of the
+    graph with no error; with it the error surfaces at the next compiled
+    call (or at ``runtime.check_status()``, which synchronises)."""
+
+    _boxed_call = True
+
+    def __init__(self, fn, device: int):
+        self.fn = fn
+        self.device = device
+
+    def __call__(self, args):
+        torch.ops.b200.status_check(self.device, False)
+        out = self.fn(args)
+        torch.ops.b200.status_check(self.device, True)
+        return out
+
+
+def _gemm_device(gm: fx.GraphModule, example_inputs) -> int | None:
+    """CUDA device index of the graph's GEMM launches, None when it has none."""
+    for n in gm.graph.nodes:
+        if n.op == "call_function" and n.target == torch.ops.b200.gemm_epilogue.default:
+            val = n.args[0].meta.get("val") if isinstance(n.args[0], fx.Node) else None
+            if isinstance(val, torch.Tensor) and val.is_cuda:
+                return val.device.index if val.device.index is not None else torch.cuda.current_device()
+            for t in example_inputs:
+                if isinstance(t, torch.Tensor) and t.is_cuda:
+                    return t.device.index if t.device.index is not None else torch.cuda.current_device()
+    return None
+
+
+def _checked(gm: fx.GraphModule, example_inputs, fn):
+    dev = _gemm_device(gm, example_inputs)
+    return fn if dev is None else StatusChecked(fn, dev)
+
+
 def compiler(gm: fx.GraphModule, example_inputs):
     """Forward and backward graphs of training: the passes, run op by op."""
-    return make_boxed_func(_passes(gm).forward)
+    gm = _passes(gm)
+    return _checked(gm, example_inputs, make_boxed_func(gm.forward))
 
 
 def inference_compiler(gm: fx.GraphModule, example_inputs):
@@ -78,7 +119,7 @@ def inference_compiler(gm: fx.GraphModule, example_inputs):
     fn = make_boxed_func(gm.forward)
     if config.EXTENSIONS:
         fn = graph_replay.wrap(gm, fn)
-    return fn
+    return _checked(gm, example_inputs, fn)
 
 
 custom_backend = aot_autograd(

@@ -52,80 +52,95 @@ _fused_counter = 0
 
 
 def _tensor_meta(node):
-    val = node.meta.get("val") if isinstance(node, fx.Node) else None
+    """The FakeTensor value AOTAutograd recorded for `node`, or None."""
+    if not isinstance(node, fx.Node):
+        return None
+    val = node.meta.get("val")
     return val if isinstance(val, torch.Tensor) else None
 
 
 def _is_float_cast(node: fx.Node) -> bool:
-    """A dtype conversion between floats that fit in fp32.  In the reference a
-    cast below fp32 must end its group: only the final store rounds, so ops
-    after it would see the unrounded value (reference :67-79).  With the
-    extensions on, the kernel rounds at the cast itself (ROUND_BF16/F16), so
-    such a cast may sit inside a group and bf16 chains like
-    cast -> gelu -> cast -> +residual stay one kernel with eager's rounding."""
+    """True for an ``aten._to_copy`` that only changes the dtype between two
+    floating types no wider than fp32.
+
+    The reference ends a group at a cast below fp32, because its kernel
+    rounds only when it stores the result and ops after the cast would see
+    the unrounded value (fusion_pointwise.py:44-58).  With the extensions on,
+    the program rounds at the cast itself (ROUND_BF16/F16), so a narrowing
+    cast may sit inside a group: bf16 chains such as cast -> gelu -> cast ->
+    +residual become one kernel with eager's rounding."""
+    if set(node.kwargs) != {"dtype"}:
+        return False
     src, dst = _tensor_meta(node.args[0]), _tensor_meta(node)
-    return (
-        set(node.kwargs) == {"dtype"}
-        and src is not None
-        and dst is not None
-        and src.is_floating_point()
-        and torch.float64 not in (src.dtype, dst.dtype)
-        and (
-            dst.dtype == torch.float32
-            or config.EXTENSIONS
-            or not any(_is_fusible(u) for u in node.users)
-        )
-    )
+    if src is None or dst is None or not src.is_floating_point():
+        return False
+    if src.dtype == torch.float64 or dst.dtype == torch.float64:
+        return False
+    if dst.dtype == torch.float32 or config.EXTENSIONS:
+        return True
+    # A narrowing cast must be the last node of its group.
+    return all(not _is_fusible(user) for user in node.users)
 
 
 def _is_fusible(node: fx.Node) -> bool:
+    """An op of POINTWISE_OPS with a floating, statically shaped result on the
+    target device (CUDA unless a test injects another predicate)."""
     if node.op != "call_function" or node.target not in POINTWISE_OPS:
         return False
-    if node.target == aten._to_copy.default:
-        if not _is_float_cast(node):
-            return False
-    elif node.kwargs:
+    args_ok = _is_float_cast(node) if node.target == aten._to_copy.default else not node.kwargs
+    if not args_ok:
         return False
     val = _tensor_meta(node)
-    return (
-        val is not None
-        and config.on_target_device(val)
-        and val.is_floating_point()
-        and all(isinstance(s, int) for s in val.shape)  # static shapes only
-    )
+    if val is None or not val.is_floating_point() or not config.on_target_device(val):
+        return False
+    return not any(isinstance(d, torch.SymInt) or not isinstance(d, int) for d in val.shape)
 
 
 def find_fusion_groups(graph: fx.Graph) -> list[list[fx.Node]]:
-    """Walk the graph backwards and pull each fusible node into its
-    consumers' group when (a) all of its users are in that one group and
-    (b) it has the group's output shape.  (a) keeps every group
-    single-output.  Groups come back in topological order (reference
-    :99-128)."""
-    group_of: dict[fx.Node, list[fx.Node]] = {}
-    for node in reversed(graph.nodes):
+    """Partition the fusible nodes of `graph` into single-output groups.
+
+    Nodes are visited from the graph's end, so every consumer is placed
+    before its producers.  A node joins the group that holds all of its
+    users when there is exactly one such group and the node's shape equals
+    that group's output shape; otherwise it opens a new group.  Because a
+    node joins only when every user is already inside, no value but the
+    group's last one is read outside it.  The grouping decisions, the order
+    of the groups (by their output node, last first) and the order inside a
+    group (graph order) are the reference's (fusion_pointwise.py:76-105);
+    tests/test_passes.py checks them against its recorded groupings.
+    """
+    group_id: dict[fx.Node, int] = {}
+    groups: list[list[fx.Node]] = []  # each filled consumers first
+    for node in reversed(list(graph.nodes)):
         if not _is_fusible(node):
             continue
-        consumer_groups = [group_of.get(u) for u in node.users]
-        group = consumer_groups[0] if consumer_groups else None
-        if (
-            group is not None
-            and all(g is group for g in consumer_groups)
-            and _tensor_meta(node).shape == _tensor_meta(group[0]).shape
-        ):
-            group.append(node)
-        else:
-            group = [node]
-        group_of[node] = group
-
-    order = {n: i for i, n in enumerate(graph.nodes)}
-    groups = {id(g): g for g in group_of.values()}.values()
-    return [sorted(g, key=order.__getitem__) for g in groups]
+        user_groups = {group_id.get(user, -1) for user in node.users}
+        joined = -1
+        if len(user_groups) == 1:
+            (gid,) = user_groups
+            if gid >= 0 and _tensor_meta(node).shape == _tensor_meta(groups[gid][0]).shape:
+                joined = gid
+        if joined < 0:
+            joined = len(groups)
+            groups.append([])
+        groups[joined].append(node)
+        group_id[node] = joined
+    return [g[::-1] for g in groups]
 
 
 def external_inputs(group: list[fx.Node]) -> list[fx.Node]:
-    """Nodes the group reads from outside, deduplicated, in first-use order."""
-    members = set(group)
-    return list(dict.fromkeys(arg for node in group for arg in node.all_input_nodes if arg not in members))
+    """The values the group reads but does not compute, each listed once, in
+    the order the group first reads them.  This order is the fused op's
+    argument order (reference fusion_pointwise.py:108-113)."""
+    inside = set(group)
+    order: list[fx.Node] = []
+    listed: set[fx.Node] = set()
+    for node in group:
+        for arg in node.all_input_nodes:
+            if arg not in inside and arg not in listed:
+                listed.add(arg)
+                order.append(arg)
+    return order
 
 
 def new_kernel_name(prefix: str) -> str:

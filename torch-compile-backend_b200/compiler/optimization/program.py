@@ -2,11 +2,13 @@
 
 The reference turns each group into Triton source, one SSA line per node
 (compiler/optimization/fusion_pointwise.py:116-129, emit_pointwise_ops), and
-JIT-compiles it.  Here a group becomes data instead: a short program for the
-accumulator machine that every pointwise and GEMM-epilogue kernel in
-libb200k.so interprets per element (include/b200k.h documents the
-instruction set).  No source is generated and nothing is compiled at run
-time.
+JIT-compiles it.  Here a group becomes a short program for an accumulator
+machine (include/b200k.h documents the instruction set), passed to the
+kernel library as data.  The library either interprets it per element (the
+GEMM epilogues outside the compiled canonical forms, and pointwise launches
+outside the generated kernels' scope) or writes it out as straight-line CUDA
+C and compiles that for sm_100a with NVRTC on first use
+(csrc/pointwise_jit.cu), once per program and operand layout.
 
 Machine model: one accumulator, ``MAX_SLOTS`` value slots.  Operands (the
 group's external inputs, or for a GEMM epilogue the accumulator and the extra

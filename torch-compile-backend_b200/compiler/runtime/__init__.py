@@ -87,3 +87,14 @@ def gemm_status(device: int = 0, reset: bool = True) -> int:
     synchronises with the device."""
     load()
     return int(torch.ops.b200.gemm_status(device, reset))
+
+
+def check_status(device: int = 0) -> None:
+    """Synchronises with the device and raises RuntimeError if a GEMM launched
+    through ``torch.ops.b200.gemm_epilogue`` reported a device-side timeout
+    since the last check (the word is then cleared)."""
+    load()
+    v = gemm_status(device, reset=True)
+    if v != 0:
+        raise RuntimeError(f"b200::gemm_epilogue on cuda:{device} reported status {v} "
+                           "(6 = a device-side wait timed out): an earlier GEMM's output is incomplete")

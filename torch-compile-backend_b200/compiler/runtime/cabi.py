@@ -29,7 +29,8 @@ GEMM_TEST_WITHHOLD_READY = 1  # include/b200k.h: failure-detection test hook
 EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
-    "b200k_gemm_epilogue_noalloc", "b200k_rope", "b200k_pointwise_jit_stats", "b200k_pointwise_jit_compile",
+    "b200k_gemm_epilogue_noalloc", "b200k_gemm_noalloc_status", "b200k_rope", "b200k_pointwise_jit_stats",
+    "b200k_pointwise_jit_compile",
 ]
 
 
@@ -112,6 +113,7 @@ def library() -> ctypes.CDLL:
             ("b200k_pointwise", [ctypes.POINTER(PointwiseArgs), ctypes.c_void_p]),
             ("b200k_gemm_epilogue", [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
             ("b200k_gemm_epilogue_noalloc", [ctypes.POINTER(GemmArgs), ctypes.c_void_p]),
+            ("b200k_gemm_noalloc_status", [ctypes.POINTER(ctypes.c_int32), ctypes.c_void_p]),
             ("b200k_rownorm", [ctypes.POINTER(RowNormArgs), ctypes.c_void_p]),
             ("b200k_softmax", [ctypes.POINTER(SoftmaxArgs), ctypes.c_void_p]),
             ("b200k_rope", [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
@@ -233,6 +235,15 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
         _check("b200k_gemm_epilogue_noalloc", library().b200k_gemm_epilogue_noalloc(ctypes.byref(g), _stream()))
     else:
         _check("b200k_gemm_epilogue", library().b200k_gemm_epilogue(ctypes.byref(g), _stream()))
+
+
+def gemm_noalloc_status() -> int:
+    """Status word of the last allocation-free GEMM on the current device
+    (0 = ok, 6 = a device-side wait timed out); synchronises with the current
+    stream."""
+    v = ctypes.c_int32(-1)
+    _check("b200k_gemm_noalloc_status", library().b200k_gemm_noalloc_status(ctypes.byref(v), _stream()))
+    return int(v.value)
 
 
 def rownorm(x: torch.Tensor, kind: int, weight, bias, eps: float, flags: int, out: torch.Tensor,

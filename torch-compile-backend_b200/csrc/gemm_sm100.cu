@@ -354,28 +354,51 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
 // ---------------------------------------------------------------------------
 static __device__ __align__(256) int32_t g_noalloc_scratch[B200K_NOALLOC_SCRATCH_BYTES / sizeof(int32_t)];
 
+namespace {
+// Device address of this device's copy of g_noalloc_scratch, looked up on the
+// first use per device with that device current.  The lookup may load the
+// library's module into the context, which is not a stream operation, so it
+// is refused while `st` is capturing (B200K_ERR_LAUNCH, nothing enqueued).
+// The cache lives for the process: cudaDeviceReset invalidates it.
+int noalloc_scratch(cudaStream_t st, void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return B200K_ERR_DEVICE;
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return B200K_ERR_LAUNCH;
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return B200K_ERR_LAUNCH;
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return B200K_OK;
+}
+}  // namespace
+
 extern "C" int b200k_gemm_epilogue_noalloc(const B200kGemmArgs* args, void* stream_) {
   if (!args) return B200K_ERR_ARG;
   const size_t need = B200K_NOALLOC_STATUS_BYTES;  // one status word per call
   if (need > sizeof(g_noalloc_scratch)) return B200K_ERR_SHAPE;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return B200K_ERR_DEVICE;
-  static std::mutex mu;
-  static void* addr[64] = {nullptr};
-  if (dev >= 64) return B200K_ERR_DEVICE;
-  void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(mu);
-    if (addr[dev] == nullptr) {
-      void* p = nullptr;
-      if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) return B200K_ERR_LAUNCH;
-      addr[dev] = p;
-    }
-    scratch = addr[dev];
-  }
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(st, &scratch);
+  if (rc != B200K_OK) return rc;
   if (cudaMemsetAsync(scratch, 0, need, st) != cudaSuccess) return B200K_ERR_LAUNCH;
   B200kGemmArgs a = *args;
   a.status = static_cast<int32_t*>(scratch);
   return b200k_gemm_epilogue(&a, stream_);
+}
+
+extern "C" int b200k_gemm_noalloc_status(int32_t* host_out, void* stream_) {
+  if (!host_out) return B200K_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  void* scratch = nullptr;
+  const int rc = noalloc_scratch(st, &scratch);
+  if (rc != B200K_OK) return rc;
+  if (cudaMemcpyAsync(host_out, scratch, sizeof(int32_t), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+    return B200K_ERR_LAUNCH;
+  return cudaStreamSynchronize(st) == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;
 }

@@ -14,6 +14,7 @@
 #include <torch/library.h>
 
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -56,6 +57,8 @@ B200kProgram make_program(at::IntArrayRef code, at::ArrayRef<double> imm) {
 void* stream_of(const at::Tensor& t) {
   return static_cast<void*>(at::cuda::getCurrentCUDAStream(t.device().index()).stream());
 }
+
+std::atomic<int64_t> g_test_stall_ns{0};
 
 // Per-device status word the GEMM kernel writes when a wait times out.
 at::Tensor& status_word(int dev) {
@@ -195,6 +198,11 @@ at::Tensor gemm_epilogue(const at::Tensor& a, const at::Tensor& b, at::TensorLis
     g.form.residual = static_cast<int32_t>(form[5]);
   }
   g.status = status_word(a.device().index()).data_ptr<int32_t>();
+  const int64_t stall = g_test_stall_ns.exchange(0);
+  if (stall > 0) {  // failure-detection test hook, armed by gemm_test_stall_next
+    g.test_flags = B200K_GEMM_TEST_WITHHOLD_READY;
+    g.timeout_ns = stall;
+  }
   check(b200k_gemm_epilogue(&g, stream_of(a)), "gemm_epilogue");
   return out;
 }
@@ -204,6 +212,71 @@ int64_t gemm_status(int64_t device, bool reset) {
   const int64_t v = w.item<int32_t>();
   if (reset) w.zero_();
   return v;
+}
+
+// Asynchronous watch of the status word for the compiled graphs.  After a
+// graph has queued its GEMMs, `status_check(dev, arm=true)` queues a copy of
+// the word into pinned host memory and an event behind them on the current
+// stream; every check first looks at the last copy whose event has
+// completed and raises when a wait timed out (then the word and the copy are
+// cleared, so each timeout is reported once).  Nothing here synchronises;
+// inside a stream capture the copy is not queued.
+struct StatusWatch {
+  int32_t* host = nullptr;
+  cudaEvent_t ev = nullptr;
+  bool armed = false;
+};
+
+int64_t status_check(int64_t device, bool arm) {
+  static std::mutex mu;
+  static std::vector<StatusWatch> watches;
+  const int dev = static_cast<int>(device);
+  c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(dev));
+  at::Tensor& word = status_word(dev);
+  cudaStream_t st = at::cuda::getCurrentCUDAStream(dev).stream();
+  int32_t seen = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (static_cast<int>(watches.size()) <= dev) watches.resize(dev + 1);
+    StatusWatch& w = watches[dev];
+    if (w.host == nullptr) {
+      TORCH_CHECK(cudaHostAlloc(reinterpret_cast<void**>(&w.host), sizeof(int32_t), cudaHostAllocDefault) ==
+                      cudaSuccess, "b200::status_check: pinned allocation failed");
+      *w.host = 0;
+      TORCH_CHECK(cudaEventCreateWithFlags(&w.ev, cudaEventDisableTiming) == cudaSuccess,
+                  "b200::status_check: event creation failed");
+    }
+    if (w.armed && cudaEventQuery(w.ev) == cudaSuccess) {
+      seen = *reinterpret_cast<volatile int32_t*>(w.host);
+      if (seen != 0) {
+        *w.host = 0;
+        w.armed = false;
+      }
+    }
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    const bool capturing = cudaStreamIsCapturing(st, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone;
+    if (seen == 0 && arm && !capturing) {
+      TORCH_CHECK(cudaMemcpyAsync(w.host, word.data_ptr<int32_t>(), sizeof(int32_t), cudaMemcpyDeviceToHost, st) ==
+                      cudaSuccess, "b200::status_check: copy failed");
+      TORCH_CHECK(cudaEventRecord(w.ev, st) == cudaSuccess, "b200::status_check: event record failed");
+      w.armed = true;
+    }
+  }
+  if (seen != 0) {
+    word.zero_();
+    TORCH_CHECK(false, "b200::gemm_epilogue on cuda:", dev, " reported ", b200k_status_string(static_cast<int>(seen)),
+                " (code ", seen, "): an earlier GEMM's output is incomplete");
+  }
+  return 0;
+}
+
+// Test hook: the next gemm_epilogue launch through this binding withholds
+// its first tile's accumulator-ready signal (B200K_GEMM_TEST_WITHHOLD_READY),
+// so the epilogue's wait runs out after `timeout_ns`.  Failure-detection
+// tests only.
+void gemm_test_stall_next(int64_t timeout_ns) {
+  TORCH_CHECK(timeout_ns > 0, "b200::gemm_test_stall_next: timeout_ns must be positive");
+  g_test_stall_ns.store(timeout_ns);
 }
 
 void rows_of(const at::Tensor& x, int64_t& rows, int64_t& cols, int64_t& row_stride) {
@@ -395,6 +468,8 @@ TORCH_LIBRARY(b200, m) {
   m.def("log_softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("rope(Tensor x, Tensor cos, Tensor sin, int[] out_stride=[]) -> Tensor");
   m.def("gemm_status(int device, bool reset) -> int", &gemm_status);
+  m.def("status_check(int device, bool arm) -> int", &status_check);
+  m.def("gemm_test_stall_next(int timeout_ns) -> ()", &gemm_test_stall_next);
 }
 
 TORCH_LIBRARY_IMPL(b200, CUDA, m) {
