@@ -1,7 +1,8 @@
 """Benchmark: fused GEMM + epilogue sweep on B200 (the headline workload).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload sweep|gemm|chain|vit|llama] [--backend ours|eager|reference_triton|inductor]
+                    [--workload sweep|gemm|chain|vit|llama|pointwise]
+                    [--backend ours|eager|reference_triton|inductor]
 
 One step of the default workload ("gemm_epilogue_sweep") runs the fused bf16
 GEMM sweep once: Y = act(X W^T + b) + R for act in {none, gelu, silu} and
@@ -13,13 +14,22 @@ custom_backend) with X and R copied in from pinned host memory and Y copied
 back inside the timed region; the copies run on two copy streams, so one
 GEMM's transfers overlap its neighbours' compute.
 
-Multi-GPU: one process per GPU (torchrun), each GPU runs the full sweep as an
-independent replica (weak scaling, no data-path collective); a gloo process
-group carries only the barrier and the max-over-ranks time.
+The same line carries the other half of the benchmark's metric: `models`
+(ViT-B/16 batch 64 and the Llama-style prefill 8 x 2048, forward tokens/s
+through this backend, eager PyTorch and, at N = 1, the reference Triton
+backend), `chain` (RMSNorm+SwiGLU and softmax GB/s) and `cpu_baseline` (the
+reference's CPU path on the host cores, N = 1).  --no-extras skips them.
 
---impl reference times the CPU implementation of the same path on the host
-cores: the oracle restatement of the reference kernels' arithmetic (numpy
-fp32 GEMM + epilogue), on a bounded row sample of every sweep GEMM.
+Multi-GPU: one process per GPU (torchrun), each GPU runs the full sweep as an
+independent replica (weak scaling, no data-path collective); the model
+extras split their batch over the GPUs.  A gloo process group carries only
+the barrier and the max-over-ranks time.  Each rank is bound to the host
+CPUs of its GPU's NUMA node.
+
+--impl reference times the reference's own CPU path of the sweep on the
+host cores: the unmodified reference backend (baseline/_ref) compiling each
+sweep block on CPU tensors, where it fuses nothing, i.e. eager PyTorch bf16
+on the same ATen graph, on a bounded row sample of every sweep GEMM.
 """
 from __future__ import annotations
 
@@ -67,33 +77,16 @@ def load_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-# Kernel and ncu summary (profiles/<name>.md) per tile config of the dominant launch.
-_DOMINANT_KERNELS = {3: ("gemm_pair_kernel 256x256", "gemm_pair_16384x4096x14336_gelu"),
-                     4: ("gemm_pair_kernel 256x512", "gemm_pair_wide_16384x4096x14336_gelu")}
+# Kernel name per tile config of the dominant launch.
+_DOMINANT_KERNELS = {3: "gemm_pair_kernel 256x256", 4: "gemm_pair_kernel 256x512"}
 
 
-def _dominant_kernel() -> tuple[str, str | None]:
-    """The kernel the library picks for the sweep's dominant launch and the
-    name of its ncu summary under profiles/ (None when there is none)."""
+def _dominant_kernel() -> tuple[str]:
+    """The kernel the library picks for the sweep's dominant launch."""
     from compiler.runtime import cabi
 
     cfg = cabi.library().b200k_gemm_pick_config(*DOMINANT)
-    return _DOMINANT_KERNELS.get(cfg, ("gemm_epilogue_kernel", None))
-
-
-def profile_traffic(name: str):
-    """Per-launch DRAM bytes recorded from an ncu capture in profiles/<name>.md
-    (line 'dram_bytes_per_launch: <int>'), or None."""
-    p = os.path.join(ROOT, "profiles", name + ".md")
-    if not os.path.exists(p):
-        return None
-    for line in open(p):
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            try:
-                return int(line.split(":", 1)[1].strip().split()[0])
-            except ValueError:
-                return None
-    return None
+    return (_DOMINANT_KERNELS.get(cfg, "gemm_epilogue_kernel"),)
 
 
 # --------------------------------------------------------------- clocks
@@ -367,7 +360,10 @@ def run_sweep(args, dist: Dist) -> dict:
     M, N, K = DOMINANT
     dom_ms = statistics.mean(per[dom])
     achieved = 2.0 * M * N * K / (dom_ms * 1e-3) / 1e12
-    peak = peaks.get("bf16_tflops_sustained", peaks["bf16_tflops"])
+    # Each launch is timed on its own (events around it), so the burst peak
+    # is the denominator; the sustained figure is reported beside it.
+    peak = peaks["bf16_tflops"]
+    sustained = peaks.get("bf16_tflops_sustained")
     sweep_detail = []
     for (M, N, K) in SWEEP:
         for act in ACTS:
@@ -394,10 +390,13 @@ def run_sweep(args, dist: Dist) -> dict:
                    "l2": "256 MB flush between steps (outside the per-launch events)",
                    "parallelism": f"replicas x{n}"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 3), "peak_source": f"{src} bf16_tflops_sustained",
-                     "frac_of_burst": round(achieved / peaks["bf16_tflops"], 3),
+                     "frac": round(achieved / peak, 3), "peak_source": f"{src} bf16_tflops (burst)",
+                     "frac_of_sustained": round(achieved / sustained, 3) if sustained else None,
                      "kernel": _dominant_kernel()[0] + " 16384x4096x14336 gelu",
-                     "traffic": profile_traffic(_dominant_kernel()[1]) if _dominant_kernel()[1] else None},
+                     "algorithmic_bytes": 2 * (M * K + N * K + 2 * M * N) + 2 * N,
+                     "traffic": None,
+                     "traffic_note": "not measured by this run (ncu cannot run inside it); the ncu "
+                                     "capture of this kernel is summarised under profiles/"},
         "e2e": {"value": round(n * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
                 "graphs_compiled": e2e_graphs},
@@ -668,38 +667,167 @@ def run_pointwise(args, dist: Dist) -> dict:
                                          "peak_source": src + " hbm_gbs"}}
 
 
-# --------------------------------------------------------------- CPU (oracle) leg
-def cpu_sweep(rows: int, reps: int) -> dict:
-    """The oracle's GEMM + epilogue (numpy fp32, every host core via BLAS) on
-    the first `rows` rows of every sweep GEMM."""
-    import numpy as np
+# --------------------------------------------------------------- CPU (reference) leg
+def _host_threads() -> int:
+    """Every host thread this process may run on (torchrun sets
+    OMP_NUM_THREADS=1 for its ranks; the CPU leg overrides it)."""
+    try:
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return n
 
-    import oracle
 
-    rng = np.random.default_rng(0)
-    gelu = [["mul.Tensor", [["acc"], 0.5]], ["mul.Tensor", [["acc"], 0.7071067811865476]],
-            ["erf.default", [["node", 1]]], ["add.Tensor", [["node", 2], 1.0]],
-            ["mul.Tensor", [["node", 0], ["node", 3]]]]
-    silu = [["sigmoid.default", [["acc"]]], ["mul.Tensor", [["acc"], ["node", 0]]]]
+def run_reference_cpu(steps: int, warmup: int, rows: int) -> dict:
+    """The reference's own CPU path for the sweep on the host cores.
+
+    Each block runs through ``torch.compile(block, backend=custom_backend)``
+    with the UNMODIFIED reference backend from baseline/_ref.  On CPU tensors
+    that backend fuses nothing (its passes require CUDA values,
+    compiler/optimization/fusion_pointwise.py:70 and fusion_epilogue.py:41-42),
+    so a step is eager PyTorch bf16 (oneDNN, AMX where the host has it) on the
+    sweep's own ATen graph, with every host thread.  A step runs the first
+    `rows` rows of each of the twelve sweep GEMMs (the 512^3 points whole);
+    the value is the sampled FLOPs / median step time.  Without the reference
+    install the same blocks run eagerly (kind "port")."""
+    from bench_models import GemmEpilogueBlock, init_sweep_block
+
+    threads = _host_threads()
+    backend, kind = None, "port"
+    try:
+        _use_reference_triton()
+        from compiler.backend import custom_backend as backend  # the reference's package
+
+        kind = "reference"
+    except Exception as e:  # noqa: BLE001 -- recorded in the line
+        print(f"reference backend unavailable ({e}); timing eager PyTorch", file=sys.stderr)
+    torch._dynamo.config.recompile_limit = max(torch._dynamo.config.recompile_limit, 64)
+    gen = torch.Generator().manual_seed(0)
     work = []
     for (M, N, K) in SWEEP:
         m = min(rows, M)
-        x = oracle.round_bf16((0.02 * rng.standard_normal((m, K))).astype(np.float32))
-        w = oracle.round_bf16((0.02 * rng.standard_normal((K, N))).astype(np.float32))
-        b = oracle.round_bf16((0.01 * rng.standard_normal(N)).astype(np.float32))
-        r = oracle.round_bf16((0.02 * rng.standard_normal((m, N))).astype(np.float32))
-        for act, spec in (("none", []), ("gelu", gelu), ("silu", silu)):
-            s = list(spec) + [["add.Tensor", [["node", len(spec) - 1] if spec else ["acc"], ["in", 1]]]]
-            work.append((x, w, b, r, s, 2.0 * m * N * K))
-    t0 = time.perf_counter()
-    for _ in range(reps):
-        for x, w, b, r, s, _ in work:
-            oracle.gemm_epilogue(x, w, s, [b, r], "bfloat16", bias=b)
-    dt = time.perf_counter() - t0
-    flops = reps * sum(f for *_, f in work)
-    return {"value": round(flops / dt / 1e12, 4), "unit": "TFLOP/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": f"first {rows} rows of each of the 12 sweep GEMMs, x{reps}; {dt:.1f} s",
-            "seconds": round(dt, 2)}
+        x = (0.02 * torch.randn(m, K, generator=gen)).to(torch.bfloat16)
+        r = (0.02 * torch.randn(m, N, generator=gen)).to(torch.bfloat16)
+        for act in ACTS:
+            blk = GemmEpilogueBlock(K, N, act)
+            init_sweep_block(blk, torch.Generator().manual_seed(len(work)))
+            blk = blk.to(torch.bfloat16).eval()
+            f = torch.compile(blk, backend=backend) if backend is not None else blk
+            work.append((f, x, r, 2.0 * m * N * K))
+    times = []
+    with torch.no_grad():
+        for _ in range(max(1, warmup)):
+            for f, x, r, _ in work:
+                f(x, r)
+        for _ in range(max(1, steps)):
+            t0 = time.perf_counter()
+            for f, x, r, _ in work:
+                f(x, r)
+            times.append(time.perf_counter() - t0)
+    flops = sum(w[3] for w in work)
+    med = statistics.median(times)
+    return {"value": round(flops / med / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind,
+            "sample": f"first {rows} rows of each of the 12 sweep GEMMs (512^3 whole), bf16, "
+                      f"median of {len(times)} steps of {med * 1e3:.0f} ms; reference backend on CPU = "
+                      "eager ATen graph", "ms_per_step": round(med * 1e3, 2)}
+
+
+def _cpu_baseline_subprocess(rows: int) -> dict | None:
+    """run_reference_cpu in a process of its own (the reference's package is
+    also named `compiler`), with no GPU visible."""
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="")
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT", "OMP_NUM_THREADS"):
+        env.pop(k, None)
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--impl", "reference", "--steps", "3", "--warmup", "1",
+           "--cpu-rows", str(rows)]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, env=env)
+        line = [ln for ln in r.stdout.splitlines() if ln.startswith("{")][-1]
+        return json.loads(line)["cpu_baseline"]
+    except Exception as e:  # noqa: BLE001
+        return {"value": None, "unavailable": f"{type(e).__name__}: {e}"[:300]}
+
+
+# --------------------------------------------------------------- model extras
+def _reference_triton_model(workload: str, batch: int, steps: int, warmup: int) -> dict:
+    """--workload vit|llama through the reference Triton backend, in a process
+    of its own; its JSON line, or the error it stopped with."""
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--workload", workload, "--backend", "reference_triton",
+           "--batch", str(batch), "--steps", str(steps), "--warmup", str(warmup)]
+    env = dict(os.environ)
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "timed out after 900 s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode == 0 and lines:
+        d = json.loads(lines[-1])
+        return {"tokens_per_s": d["value"], "ms": d["ms_per_step"], "compile_s": d.get("compile_s")}
+    err = [ln for ln in r.stderr.splitlines() if "Error" in ln or "error" in ln]
+    return {"unavailable": (err[-1] if err else f"exit code {r.returncode}")[:300]}
+
+
+def run_model_extras(args, dist: Dist) -> dict:
+    """ViT-B/16 (batch 64) and the Llama-style prefill (8 x 2048) forward,
+    split by batch over the N GPUs (64/N images, 8/N sequences per GPU;
+    strong scaling), this backend and eager PyTorch on each GPU; tokens/s =
+    all ranks' tokens / the slowest rank's median step.  At N = 1 the
+    reference Triton backend runs the same configs in a subprocess."""
+    out = {}
+    for wl, full in (("vit", 64), ("llama", 8)):
+        per = max(1, full // dist.world)
+        res = {"batch_per_gpu": per, "global_batch": per * dist.world}
+        for be in ("ours", "eager"):
+            ns = argparse.Namespace(workload=wl, backend=be, batch=per, steps=args.model_steps,
+                                    warmup=max(3, args.warmup))
+            torch._dynamo.reset()
+            dist.barrier()
+            d = run_model(ns, dist)
+            ms = dist.max(d["ms_per_step"])
+            tokens = d["config"]["tokens"] * dist.world
+            res[be] = {"tokens_per_s": round(tokens / (ms * 1e-3), 1), "ms": round(ms, 3),
+                       "tflops": round(d["tflops"] * dist.world * d["ms_per_step"] / ms, 1)}
+            if be == "ours":
+                from compiler import runtime
+
+                runtime.check_status(dist.local)
+        if dist.world == 1 and args.reference_models:
+            res["reference_triton"] = _reference_triton_model(wl, per, args.model_steps, max(3, args.warmup))
+        out[wl] = res
+    torch._dynamo.reset()
+    return out
+
+
+def run_chain_extra(args, dist: Dist) -> dict:
+    ns = argparse.Namespace(workload="chain", backend="ours", steps=args.model_steps, warmup=max(3, args.warmup))
+    torch._dynamo.reset()
+    d = run_chain(ns, dist)
+    return {"GB/s": d["value"], "frac": d["roofline"]["frac"], "kernels": d["kernels"]}
+
+
+def bind_to_gpu_numa(local: int) -> list[int] | None:
+    """Restrict this rank to the host CPUs local to its GPU (sysfs
+    local_cpulist of the GPU's PCI device), so that its pinned host buffers
+    are first touched on the GPU's own NUMA node.  Returns the CPUs, or None
+    when the topology is not readable."""
+    try:
+        prop = torch.cuda.get_device_properties(local)
+        bus = f"{prop.pci_domain_id:04x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        with open(f"/sys/bus/pci/devices/{bus}/local_cpulist") as f:
+            spec = f.read().strip()
+        cpus = []
+        for part in spec.split(","):
+            a, _, b = part.partition("-")
+            cpus.extend(range(int(a), int(b or a) + 1))
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+            return cpus
+    except (OSError, ValueError, AttributeError):
+        pass
+    return None
 
 
 def main() -> None:
@@ -718,7 +846,12 @@ def main() -> None:
     ap.add_argument("--interpret", action="store_true", help="gemm workload: interpret the epilogue program")
     ap.add_argument("--plain", action="store_true",
                     help="gemm workload: out = x w^T with no epilogue, against torch.mm in the eager leg")
-    ap.add_argument("--cpu-rows", type=int, default=256)
+    ap.add_argument("--cpu-rows", type=int, default=1024, help="rows of each sweep GEMM the CPU leg runs")
+    ap.add_argument("--model-steps", type=int, default=10, help="timed steps of each model extra")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="sweep only: skip the ViT/Llama/chain extras and the CPU baseline")
+    ap.add_argument("--no-reference-models", dest="reference_models", action="store_false",
+                    help="skip the reference Triton backend's ViT/Llama runs in the extras")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
@@ -727,11 +860,13 @@ def main() -> None:
     if args.impl == "reference":
         if dist_env_rank != 0:
             return
-        base = cpu_sweep(args.cpu_rows, max(1, args.steps // 5))
+        base = run_reference_cpu(args.steps, args.warmup, args.cpu_rows)
         line = {"impl": "reference", "metric": "fused GEMM+epilogue TFLOP/s", "value": base["value"],
                 "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-                "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic", "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS},
+                "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) X/W/R, N(0,0.01) b)",
+                "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS,
+                           "epilogue": "act(X W^T + b) + R, bf16 in/out", "sample_rows": args.cpu_rows},
                 "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
                 "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
@@ -740,6 +875,7 @@ def main() -> None:
 
     dist = Dist()
     try:
+        cpus = bind_to_gpu_numa(dist.local) if torch.cuda.is_available() else None
         if args.workload == "gemm":
             print(json.dumps(run_single_gemm(args, dist)))
             return
@@ -753,10 +889,13 @@ def main() -> None:
             print(json.dumps(run_pointwise(args, dist)))
             return
         res = run_sweep(args, dist)
+        res["host_cpus_bound"] = len(cpus) if cpus else None
+        if not args.no_extras:
+            res["models"] = run_model_extras(args, dist)
+            res["chain"] = run_chain_extra(args, dist)
         if dist.rank == 0:
-            if dist.world == 1:
-                base = cpu_sweep(args.cpu_rows, 1)
-                res["cpu_baseline"] = {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            if dist.world == 1 and not args.no_extras:
+                res["cpu_baseline"] = _cpu_baseline_subprocess(args.cpu_rows)
             print(json.dumps(res))
     finally:
         dist.close()
