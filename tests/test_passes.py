@@ -480,3 +480,23 @@ def test_patchify_leaves_overlapping_convolutions():
 
     (gm,) = fused_graphs(Conv().to(torch.bfloat16), (torch.randn(1, 3, 16, 16).to(torch.bfloat16),))
     assert torch.ops.aten.convolution.default in [n.target for n in gm.graph.nodes if n.op == "call_function"]
+
+
+def test_epilogue_profitability_rule():
+    """The measured cost model: fused wherever the benchmark and model
+    shapes put a pointwise tail on a GEMM; cuBLAS plus a separate kernel for
+    a deep GEMM whose tail is too small to pay for the library's gap."""
+    from compiler.optimization.fusion_epilogue import fusion_pays
+
+    bf = 2
+    # the sweep's points (bias + act + bf16 residual)
+    for M, N, K in [(512, 512, 512), (4096, 4096, 4096), (8192, 8192, 8192), (16384, 4096, 14336)]:
+        assert fusion_pays(M, N, K, bf, bf, M * N * bf + N * bf)
+    # ViT fc1 (bias + GELU), fc2 / proj (bias + residual); Llama gate (x up), down (+ residual)
+    assert fusion_pays(12608, 3072, 768, bf, bf, 3072 * bf)
+    assert fusion_pays(12608, 768, 3072, bf, bf, 12608 * 768 * bf + 768 * bf)
+    assert fusion_pays(16384, 8192, 2048, bf, bf, 16384 * 8192 * bf)
+    assert fusion_pays(16384, 2048, 8192, bf, bf, 16384 * 2048 * bf)
+    # a deep GEMM with an activation alone: the tail (one 33 MB round trip)
+    # is smaller than the library's 6 % gap on 550 GFLOP
+    assert not fusion_pays(4096, 4096, 16384, bf, bf, 0)

@@ -177,12 +177,53 @@ def epilogue_form(prog, n_operands: int, operands=None) -> list[int]:
     return form or []
 
 
+# Cost model of the profitability rule, measured on one B200 (bf16, device
+# time with CUDA-graph replay).  The library's GEMM against cuBLAS on the
+# same plain problems: 16384x2048x2048 95.4 vs 97.4 us, 16384x8192x2048
+# 364.8 vs 360.9, 12608x2304x768 (+bias) 42.2 vs 38.3, 8192^3 723.5 vs
+# 681.6, 16384x128256x2048 6281 vs 6014.
+GEMM_FLOPS = 1.5e15  # cuBLAS bf16 on large problems, FLOP/s
+HBM_BYTES = 6.5e12   # measured copy bandwidth, B/s
+LAUNCH_S = 4e-6      # one more kernel in a replayed graph
+
+
+def library_over_cublas(K: int) -> float:
+    """Measured time ratio of the library GEMM to cuBLAS by reduction depth:
+    short main loops (K <= 1024) leave the library's per-tile latencies
+    unhidden; from K = 4096 cuBLAS's 2x1 CTA-pair clusters share operands
+    the library's pairs do not."""
+    if K <= 1024:
+        return 1.10
+    return 1.0 if K < 4096 else 1.06
+
+
+def fusion_pays(M: int, N: int, K: int, acc_bytes: int, out_bytes: int, extra_bytes: int) -> bool:
+    """Predicted fused time <= predicted unfused time.  Unfused, ATen runs
+    the GEMM (cuBLAS), which writes the M x N product, and then the
+    pointwise group's kernel, which reads it back with the extra operands
+    and writes the output.  Fused, the library's GEMM (its time ratio to
+    cuBLAS above) applies the group in its epilogue; the extra operands are
+    read under the MMAs."""
+    t_mm = 2.0 * M * N * K / GEMM_FLOPS
+    tail = (2.0 * M * N * acc_bytes + M * N * out_bytes + extra_bytes) / HBM_BYTES + LAUNCH_S
+    return library_over_cublas(K) * t_mm <= t_mm + tail
+
+
 def _epilogue_is_faster(group, matmul, inputs) -> bool:
     """Profitability rule standing in for the reference's compile-time
-    wall-clock race (:207-234).  The fused kernel does the same tensor-core
-    work as the library GEMM and saves one M x N write and re-read plus a
-    launch, so it is taken whenever the kernel supports the shapes."""
-    return True
+    wall-clock race (:207-234): the cost model of ``fusion_pays`` on the
+    group's shapes and dtypes."""
+    mat1, mat2 = matmul.args[-2:]
+    a, b, acc = _tensor_meta(mat1), _tensor_meta(mat2), _tensor_meta(matmul)
+    out = _tensor_meta(group[-1])
+    M, K = a.shape
+    N = b.shape[1]
+    extra = 0
+    for n in inputs:
+        v = _tensor_meta(n)
+        if v is not None:
+            extra += v.numel() * v.element_size()
+    return fusion_pays(int(M), int(N), int(K), acc.element_size(), out.element_size(), extra)
 
 
 def fuse_epilogue(gm: fx.GraphModule) -> fx.GraphModule:

@@ -34,8 +34,8 @@ CUtensorMapDataType tma_dtype(int dt) {
 
 // 2-d tiled map over a row-major view: `inner` elements contiguous, `outer`
 // rows `row_bytes` apart; box = box_inner x box_outer; 128-byte swizzle.
-bool make_map(CUtensorMap* map, int dt, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
-              uint32_t box_inner, uint32_t box_outer) {
+bool encode_map(CUtensorMap* map, int dt, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+                uint32_t box_inner, uint32_t box_outer) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {inner, outer};
@@ -45,6 +45,101 @@ bool make_map(CUtensorMap* map, int dt, const void* ptr, uint64_t inner, uint64_
   return fn(map, tma_dtype(dt), 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Host cost per launch: a model's compiled graph calls the same GEMMs on the
+// same buffers (weights, the caching allocator's recycled activations) over
+// and over, so the encoded tensor maps and the verified epilogue forms are
+// kept in small direct-mapped caches keyed on everything they depend on
+// (a map is a pure function of its arguments; it holds no device state).
+struct MapKey {
+  const void* ptr;
+  uint64_t inner, outer, row_bytes;
+  uint32_t box_inner, box_outer;
+  int32_t dt;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && inner == o.inner && outer == o.outer && row_bytes == o.row_bytes &&
+           box_inner == o.box_inner && box_outer == o.box_outer && dt == o.dt;
+  }
+};
+
+inline uint64_t mix64(uint64_t h, uint64_t v) {
+  h ^= v + 0x9e3779b97f4a7c15ull + (h << 6) + (h >> 2);
+  return h;
+}
+
+bool make_map(CUtensorMap* map, int dt, const void* ptr, uint64_t inner, uint64_t outer, uint64_t row_bytes,
+              uint32_t box_inner, uint32_t box_outer) {
+  constexpr int kSlots = 512;
+  struct Slot {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+  };
+  static Slot slots[kSlots];
+  static std::mutex mu;
+  const MapKey key{ptr, inner, outer, row_bytes, box_inner, box_outer, dt};
+  uint64_t h = reinterpret_cast<uint64_t>(ptr);
+  for (uint64_t v : {inner, outer, row_bytes, static_cast<uint64_t>(box_inner) << 32 | box_outer,
+                     static_cast<uint64_t>(dt)})
+    h = mix64(h, v);
+  Slot& slot = slots[h % kSlots];
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (slot.used && slot.key == key) {
+      *map = slot.map;
+      return true;
+    }
+  }
+  if (!encode_map(map, dt, ptr, inner, outer, row_bytes, box_inner, box_outer)) return false;
+  std::lock_guard<std::mutex> lock(mu);
+  slot.key = key;
+  slot.map = *map;
+  slot.used = true;
+  return true;
+}
+
+// check_form with a cache of the (program, form, operand count) triples that
+// passed: the probe evaluation runs once per distinct epilogue.
+int check_form_cached(const B200kEpilogueForm& f, const B200kProgram& prog, int n_extras) {
+  constexpr int kSlots = 256;
+  struct Slot {
+    B200kEpilogueForm form;
+    B200kProgram prog;
+    int n_extras;
+    bool used;
+  };
+  static Slot slots[kSlots];
+  static std::mutex mu;
+  const int n = std::max(0, std::min<int>(prog.n, B200K_MAX_INSTR));
+  uint64_t h = mix64(static_cast<uint64_t>(n_extras), static_cast<uint64_t>(n));
+  for (int i = 0; i < n; ++i) {
+    uint32_t bits;
+    std::memcpy(&bits, &prog.ins[i].imm, 4);
+    h = mix64(h, static_cast<uint64_t>(static_cast<uint32_t>(prog.ins[i].code)) << 32 | bits);
+  }
+  for (int v : {f.kind, f.bias, f.act, f.round, f.scale, f.residual}) h = mix64(h, static_cast<uint64_t>(v + 2));
+  Slot& slot = slots[h % kSlots];
+  auto same = [&](const Slot& s) {
+    if (!s.used || s.n_extras != n_extras || s.prog.n != prog.n) return false;
+    if (std::memcmp(&s.form, &f, sizeof(f)) != 0) return false;
+    return std::memcmp(s.prog.ins, prog.ins, sizeof(B200kInstr) * n) == 0;
+  };
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (same(slot)) return B200K_OK;
+  }
+  const int rc = check_form(f, prog, n_extras);
+  if (rc == B200K_OK) {
+    std::lock_guard<std::mutex> lock(mu);
+    slot.form = f;
+    std::memset(&slot.prog, 0, sizeof(slot.prog));
+    slot.prog.n = prog.n;
+    std::memcpy(slot.prog.ins, prog.ins, sizeof(B200kInstr) * n);
+    slot.n_extras = n_extras;
+    slot.used = true;
+  }
+  return rc;
 }
 
 template <int BN, int STAGES>
@@ -191,7 +286,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   int rc = validate_program(a->program, 1 + a->n_extras);
   if (rc != B200K_OK) return rc;
   if (a->form.kind != 0) {
-    rc = check_form(a->form, a->program, a->n_extras);
+    rc = check_form_cached(a->form, a->program, a->n_extras);
     if (rc != B200K_OK) return rc;
   }
 
