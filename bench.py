@@ -667,6 +667,49 @@ def run_pointwise(args, dist: Dist) -> dict:
                                          "peak_source": src + " hbm_gbs"}}
 
 
+def run_attention(args, dist: Dist) -> dict:
+    """The attention kernel alone (torch.ops.b200.attention) against PyTorch's
+    SDPA (cuDNN / flash) on the two model configs: the Llama prefill's causal
+    grouped-query attention [8, 32 / 8 heads, 2048, 64] and ViT-B/16's
+    [64, 12, 197, 64].  TFLOP/s counts the unmasked products only
+    (4 B H L S D, halved for the causal mask)."""
+    _use_ours()
+    import torch.nn.functional as F
+
+    from compiler import runtime
+
+    runtime.load()
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    out = {}
+    for name, (B, H, Hkv, L, causal) in (("llama_prefill", (8, 32, 8, 2048, True)),
+                                         ("vit_b16", (64, 12, 12, 197, False))):
+        def mk(h):  # [B, S, H, D] memory, viewed [B, H, S, D] (the models' projections)
+            return torch.randn(B, L, h, 64, device=dev, generator=gen).to(torch.bfloat16).transpose(1, 2)
+
+        q, k, v = mk(H), mk(Hkv), mk(Hkv)
+        stride = list(torch.empty(B, L, H, 64).transpose(1, 2).stride())
+        flops = 4.0 * B * H * L * L * 64 * (0.5 if causal else 1.0)
+        ours = statistics.median(_time_device(lambda: torch.ops.b200.attention(q, k, v, causal, -1.0, stride),
+                                              args.steps, args.warmup, flush))
+        theirs = statistics.median(_time_device(
+            lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal, enable_gqa=H != Hkv),
+            args.steps, args.warmup, flush))
+        runtime.check_status(dist.local)
+        out[name] = {"ms": round(ours, 4), "tflops": round(flops / (ours * 1e-3) / 1e12, 1),
+                     "sdpa_ms": round(theirs, 4), "sdpa_tflops": round(flops / (theirs * 1e-3) / 1e12, 1)}
+    peaks, src = load_peaks()
+    ll = out["llama_prefill"]
+    return {"metric": "attention TFLOP/s", "value": ll["tflops"], "unit": "TFLOP/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ll["ms"], "higher_is_better": True,
+            "dtype": "bf16", "data": "synthetic N(0,1)", "config": {"workload": "attention"}, "kernels": out,
+            "roofline": {"bound": "tensor", "achieved": ll["tflops"], "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(ll["tflops"] / peaks["bf16_tflops"], 3),
+                         "peak_source": src + " bf16_tflops (burst)"}}
+
+
 # --------------------------------------------------------------- CPU (reference) leg
 def _host_threads() -> int:
     """Every host thread this process may run on (torchrun sets
@@ -836,7 +879,8 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="sweep", choices=["sweep", "gemm", "vit", "llama", "chain", "pointwise"])
+    ap.add_argument("--workload", default="sweep",
+                    choices=["sweep", "gemm", "vit", "llama", "chain", "pointwise", "attention"])
     ap.add_argument("--backend", default="ours", choices=["ours", "eager", "reference_triton", "inductor"],
                     help="vit/llama/chain workloads: which torch.compile backend runs the model")
     ap.add_argument("--batch", type=int, default=0, help="vit/llama batch (default: the benchmark config)")
@@ -887,6 +931,9 @@ def main() -> None:
             return
         if args.workload == "pointwise":
             print(json.dumps(run_pointwise(args, dist)))
+            return
+        if args.workload == "attention":
+            print(json.dumps(run_attention(args, dist)))
             return
         res = run_sweep(args, dist)
         res["host_cpus_bound"] = len(cpus) if cpus else None

@@ -382,6 +382,47 @@ typedef struct {
 
 int b200k_rope(const B200kRopeArgs* args, void* stream);
 
+/*
+ * Fused attention forward (an extension: the reference leaves
+ * aten._scaled_dot_product_{flash,cudnn,efficient}_attention to ATen --
+ * compiler/optimization/fusion_pointwise.py:12-30 has no attention op):
+ *   out[b, h, i, :] = softmax_j(scale * q[b, h, i, :] . k[b, h / G, j, :]) v[b, h / G, j, :]
+ * with G = heads / kv_heads (grouped-query attention; G = 1 for plain
+ * multi-head attention) and, when `causal` is set, j restricted to j <= i
+ * (the top-left aligned mask of torch SDPA's is_causal).  q, k, v, out are
+ * bf16 or f16 (all the same), head_dim 64, element strides per [b, h, s, d]
+ * with unit d stride, other strides multiples of 8 elements and 16-byte
+ * aligned pointers (tensor-memory-access tiles).  Scores and the softmax run
+ * in fp32; the probabilities are rounded to the input type for the second
+ * product, as the flash kernels do.  `status`, when not NULL, receives
+ * B200K_ERR_TIMEOUT if a device-side wait runs out (timeout_ns, 0 = 2 s).
+ */
+typedef struct {
+  int64_t batch, heads, kv_heads, q_len, kv_len, head_dim;
+  const void* q;
+  int64_t q_strides[4];
+  const void* k;
+  int64_t k_strides[4];
+  const void* v;
+  int64_t v_strides[4];
+  void* out;
+  int64_t out_strides[4];
+  int32_t dtype;  /* B200K_BF16 or B200K_F16 */
+  int32_t causal;
+  float scale;    /* <= 0: 1 / sqrt(head_dim) */
+  int32_t test_flags; /* B200K_ATTN_TEST_* hooks (0 in production) */
+  int32_t* status;
+  int64_t timeout_ns;
+} B200kAttentionArgs;
+/* Test hook (test_flags bit): the MMA thread does not signal the first
+ * score block of the first query tile as ready, so the softmax's wait on it
+ * runs out after timeout_ns; the kernel reports B200K_ERR_TIMEOUT in the
+ * status word, drains, frees its tensor memory and returns (no fault).
+ * Failure-detection tests only. */
+#define B200K_ATTN_TEST_WITHHOLD_SCORES 1
+
+int b200k_attention(const B200kAttentionArgs* args, void* stream);
+
 const char* b200k_status_string(int code);
 /* Library version, for the loader's sanity check. */
 int b200k_version(void);

@@ -112,7 +112,41 @@ STRUCTS = {
     "B200kSoftmaxArgs": (cabi.SoftmaxArgs, ["rows", "x", "log_softmax", "out", "out_dtype"]),
     "B200kRopeArgs": (cabi.RopeArgs, ["sizes", "x", "x_strides", "cos", "cos_strides", "sin", "sin_strides", "out",
                                       "out_strides", "dtype"]),
+    "B200kAttentionArgs": (cabi.AttentionArgs, ["batch", "head_dim", "q", "q_strides", "k", "k_strides", "v",
+                                                "v_strides", "out", "out_strides", "dtype", "causal", "scale",
+                                                "test_flags", "status", "timeout_ns"]),
 }
+
+
+def test_attention_host_checks():
+    """Argument errors the library reports before launching anything."""
+    lib = cabi.library()
+    a = cabi.AttentionArgs()
+    a.batch, a.heads, a.kv_heads, a.q_len, a.kv_len, a.head_dim = 1, 4, 2, 16, 16, 64
+    assert lib.b200k_attention(None, None) == 1  # B200K_ERR_ARG
+    assert lib.b200k_attention(ctypes.byref(a), None) == 1  # null pointers
+    a.q = a.k = a.v = a.out = 4096
+    for st in (a.q_strides, a.k_strides, a.v_strides, a.out_strides):
+        st[0], st[1], st[2], st[3] = 4 * 16 * 64, 16 * 64, 64, 1
+    a.head_dim = 128
+    assert lib.b200k_attention(ctypes.byref(a), None) == 4  # head_dim 64 only
+    a.head_dim = 64
+    a.dtype = cabi.F32
+    assert lib.b200k_attention(ctypes.byref(a), None) == 4  # 16-bit only
+    a.dtype = cabi.BF16
+    a.kv_heads = 3
+    assert lib.b200k_attention(ctypes.byref(a), None) == 3  # heads % kv_heads
+    a.kv_heads = 2
+    a.q_strides[3] = 2
+    assert lib.b200k_attention(ctypes.byref(a), None) == 4  # unit d stride
+    a.q_strides[3] = 1
+    a.k_strides[2] = 65
+    assert lib.b200k_attention(ctypes.byref(a), None) == 2  # 16-byte rows
+    a.k_strides[2] = 64
+    a.q = 4098
+    assert lib.b200k_attention(ctypes.byref(a), None) == 2  # 16-byte pointers
+    a.q_len = 0
+    assert lib.b200k_attention(ctypes.byref(a), None) == 0  # empty output: nothing to launch
 
 
 def test_ctypes_layout_matches_c():

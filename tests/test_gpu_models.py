@@ -67,6 +67,7 @@ def test_vit_block_stack_bf16():
     # proj+res, fc1+gelu, fc2+res per block; qkv (bias only, no pointwise tail) stays cuBLAS
     assert t.count("b200.gemm_epilogue.default") == 3 * 2
     assert "b200.layer_norm.default" in t
+    assert t.count("b200.attention.default") == 2  # one per block (the tcgen05 attention kernel)
     runtime.check_status()
     ops = [n.target for g in graphs for n in g.graph.nodes if n.op == "call_function"]
     assert torch.ops.aten.convolution.default not in ops  # patch embedding lowered to a GEMM
@@ -87,6 +88,7 @@ def test_llama_small_bf16():
     t = [str(s) for s in b200_targets(graphs)]
     assert "b200.rms_norm.default" in t
     assert t.count("b200.rope.default") == 2 * 2  # q and k rotations per layer
+    assert t.count("b200.attention.default") == 2  # causal grouped-query attention per layer
     # per layer: o + residual, gate (silu * up), down + residual, all on the compiled path
     epi = [n for g in graphs for n in g.graph.nodes if n.op == "call_function"
            and n.target == torch.ops.b200.gemm_epilogue.default]

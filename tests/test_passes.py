@@ -500,3 +500,28 @@ def test_epilogue_profitability_rule():
     # a deep GEMM with an activation alone: the tail (one 33 MB round trip)
     # is smaller than the library's 6 % gap on 550 GFLOP
     assert not fusion_pays(4096, 4096, 16384, bf, bf, 0)
+
+
+def test_attention_pass_rewrites_sdpa_nodes():
+    """ViT's and the Llama block's scaled-dot-product attention become
+    b200.attention nodes (causal flag, default scale, the replaced node's
+    output layout); head_dim other than 64 stays in ATen."""
+    import bench_models as bm
+
+    torch.manual_seed(0)
+    vit = bm.ViT(depth=1).to(torch.bfloat16).eval()
+    (g,) = fused_graphs(vit, [torch.randn(2, 3, 224, 224).to(torch.bfloat16)])
+    att = [n for n in g.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.attention.default]
+    assert len(att) == 1 and att[0].args[3] is False and att[0].args[4] == -1.0
+    assert list(att[0].meta["val"].stride()) == list(att[0].args[5])
+
+    llama = bm.Llama(vocab=256, dim=256, layers=2, heads=4, kv_heads=2, ffn=256, max_seq=64).to(torch.bfloat16).eval()
+    (g,) = fused_graphs(llama, [torch.randint(0, 256, (2, 64))])
+    att = [n for n in g.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.attention.default]
+    assert len(att) == 2 and all(n.args[3] is True for n in att)
+    q, k = (n.meta["val"] for n in att[0].args[:2])
+    assert q.shape[1] == 4 and k.shape[1] == 2  # grouped-query heads passed through
+
+    small = bm.Llama(vocab=256, dim=128, layers=1, heads=4, kv_heads=2, ffn=256, max_seq=64).to(torch.bfloat16).eval()
+    (g,) = fused_graphs(small, [torch.randint(0, 256, (2, 64))])
+    assert not any(n.target == torch.ops.b200.attention.default for n in g.graph.nodes if n.op == "call_function")

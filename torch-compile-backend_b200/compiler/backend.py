@@ -20,6 +20,7 @@ from torch._functorch.aot_autograd import make_boxed_func
 from compiler import graph_replay, runtime
 from compiler.optimization import config
 from compiler.optimization.cat_inputs import contiguous_cat_inputs
+from compiler.optimization.fusion_attention import fuse_attention
 from compiler.optimization.fusion_epilogue import fuse_epilogue
 from compiler.optimization.fusion_patchify import fuse_patchify
 from compiler.optimization.fusion_pointwise import fuse_pointwise
@@ -53,6 +54,8 @@ def _passes(gm: fx.GraphModule) -> fx.GraphModule:
     if config.EXTENSIONS and config.ENABLE_ROWREDUCE:
         gm = fuse_rowreduce(gm)  # whole row groups (extension; runs first so the
         #                          pointwise passes do not split them)
+    if config.EXTENSIONS and config.ENABLE_ATTENTION:
+        gm = fuse_attention(gm)  # SDPA nodes -> the tcgen05 attention kernel (extension)
     if config.EXTENSIONS and config.ENABLE_ROPE:
         gm = fuse_rope(gm)  # x*cos + rotate_half(x)*sin (extension; before the
         #                     pointwise pass would take its multiply-add)

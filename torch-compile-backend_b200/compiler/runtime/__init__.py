@@ -75,6 +75,12 @@ def _register_fakes() -> None:
     def _(x, dim, half_to_float):
         return x.new_empty(x.shape, dtype=torch.float32 if half_to_float else x.dtype)
 
+    @torch.library.register_fake(lib + "attention")
+    def _(q, k, v, causal, scale, out_stride=()):
+        if out_stride:
+            return q.new_empty_strided(q.shape, out_stride)
+        return q.new_empty(q.shape)
+
     @torch.library.register_fake(lib + "rope")
     def _(x, cos, sin, out_stride=()):
         if out_stride:

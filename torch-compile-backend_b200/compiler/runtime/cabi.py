@@ -30,7 +30,7 @@ EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
     "b200k_gemm_epilogue_noalloc", "b200k_gemm_noalloc_status", "b200k_rope", "b200k_pointwise_jit_stats",
-    "b200k_pointwise_jit_compile",
+    "b200k_pointwise_jit_compile", "b200k_attention",
 ]
 
 
@@ -100,6 +100,19 @@ class RopeArgs(ctypes.Structure):
                 ("dtype", ctypes.c_int32), ("pad", ctypes.c_int32)]
 
 
+class AttentionArgs(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("kv_heads", ctypes.c_int64),
+                ("q_len", ctypes.c_int64), ("kv_len", ctypes.c_int64), ("head_dim", ctypes.c_int64),
+                ("q", ctypes.c_void_p), ("q_strides", ctypes.c_int64 * 4),
+                ("k", ctypes.c_void_p), ("k_strides", ctypes.c_int64 * 4),
+                ("v", ctypes.c_void_p), ("v_strides", ctypes.c_int64 * 4),
+                ("out", ctypes.c_void_p), ("out_strides", ctypes.c_int64 * 4),
+                ("dtype", ctypes.c_int32), ("causal", ctypes.c_int32), ("scale", ctypes.c_float),
+                ("test_flags", ctypes.c_int32), ("status", ctypes.c_void_p), ("timeout_ns", ctypes.c_int64)]
+
+
+ATTN_TEST_WITHHOLD_SCORES = 1  # include/b200k.h: failure-detection test hook
+
 _lib = None
 
 
@@ -117,6 +130,7 @@ def library() -> ctypes.CDLL:
             ("b200k_rownorm", [ctypes.POINTER(RowNormArgs), ctypes.c_void_p]),
             ("b200k_softmax", [ctypes.POINTER(SoftmaxArgs), ctypes.c_void_p]),
             ("b200k_rope", [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
+            ("b200k_attention", [ctypes.POINTER(AttentionArgs), ctypes.c_void_p]),
             ("b200k_gemm_pick_config", [ctypes.c_int64, ctypes.c_int64, ctypes.c_int64]),
             ("b200k_gemm_config_info", [ctypes.c_int] + [ctypes.POINTER(ctypes.c_int)] * 4),
             ("b200k_gemm_num_configs", []),
@@ -294,3 +308,24 @@ def rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tenso
     a.x, a.cos, a.sin, a.out = x.data_ptr(), c.data_ptr(), sn.data_ptr(), out.data_ptr()
     a.dtype = DTYPE[x.dtype]
     _check("b200k_rope", library().b200k_rope(ctypes.byref(a), _stream()))
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, causal: bool = False,
+              scale: float = 0.0, status: torch.Tensor | None = None, timeout_ns: int = 0,
+              test_flags: int = 0) -> None:
+    """out = softmax(scale q k^T [causal mask]) v over [B, H, S, D] views
+    (k, v with H / G heads)."""
+    a = AttentionArgs()
+    a.batch, a.heads, a.q_len, a.head_dim = q.shape
+    a.kv_heads, a.kv_len = k.shape[1], k.shape[2]
+    for dst, t in ((a.q_strides, q), (a.k_strides, k), (a.v_strides, v), (a.out_strides, out)):
+        for d in range(4):
+            dst[d] = t.stride(d)
+    a.q, a.k, a.v, a.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    a.dtype = DTYPE[q.dtype]
+    a.causal = 1 if causal else 0
+    a.scale = scale
+    a.test_flags = test_flags
+    a.status = status.data_ptr() if status is not None else None
+    a.timeout_ns = timeout_ns
+    _check("b200k_attention", library().b200k_attention(ctypes.byref(a), _stream()))

@@ -34,7 +34,7 @@ BUILD_DIR = os.path.join(PKG, "_build")
 # (tile width, activation) that has compiled-epilogue kernels; the
 # activations are B200K_ACT_NONE, GELU_ERF, GELU_TANH, SILU, RELU.
 CU_UNITS = [(src, os.path.splitext(src)[0], []) for src in ("capi.cu", "pointwise.cu", "pointwise_jit.cu", "rowreduce.cu", "rowreduce16.cu",
-                                                                  "rope.cu", "gemm_sm100.cu")]
+                                                                  "rope.cu", "gemm_sm100.cu", "attention.cu")]
 CU_UNITS += [("gemm_fast.cu", f"gemm_fast_{bn}_{act}", [f"-DB200K_FAST_BN={bn}", f"-DB200K_FAST_ACT={act}"])
              for bn in (256, 192, 128) for act in (0, 1, 2, 3, 4)]
 # ... and once per activation for the CTA-pair kernels (2: 256 x 256 tiles,

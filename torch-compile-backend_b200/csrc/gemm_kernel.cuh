@@ -1021,13 +1021,13 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
           }
         }
       }
-      if (!ok) {
-        // Let every load still in flight land before the CTA can exit.
-        for (int x = 0; x < STAGES; ++x) {
-          if (issued > x) {
-            const uint32_t par = (x < s) ? ph : (ph ^ 1u);
-            wait_bar_drain(&full[x], par, 100000000ull);
-          }
+      // Every load lands before the CTA can exit: after a timeout the MMA
+      // thread may not have waited for the last ones (otherwise these phases
+      // are complete already and the waits return at once).
+      for (int x = 0; x < STAGES; ++x) {
+        if (issued > x) {
+          const uint32_t par = (x < s) ? ph : (ph ^ 1u);
+          wait_bar_drain(&full[x], par, 100000000ull);
         }
       }
     }

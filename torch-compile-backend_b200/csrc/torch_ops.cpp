@@ -450,6 +450,45 @@ at::Tensor rope(const at::Tensor& x, const at::Tensor& cos, const at::Tensor& si
   return out;
 }
 
+// Fused attention over [B, H, S, D] views; the output gets `out_stride`
+// (the replaced SDPA node's layout) or is contiguous.
+at::Tensor attention(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool causal, double scale,
+                     at::IntArrayRef out_stride) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(), "b200::attention: q, k, v must be CUDA tensors");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "b200::attention: q, k, v must be [B, H, S, D]");
+  TORCH_CHECK(q.scalar_type() == k.scalar_type() && q.scalar_type() == v.scalar_type(),
+              "b200::attention: q, k, v dtypes differ");
+  TORCH_CHECK(k.sizes() == v.sizes(), "b200::attention: k and v shapes differ");
+  TORCH_CHECK(q.size(0) == k.size(0) && q.size(3) == k.size(3), "b200::attention: q ", q.sizes(), " and k ",
+              k.sizes(), " do not match");
+  TORCH_CHECK(out_stride.empty() || out_stride.size() == 4, "b200::attention: out_stride needs 4 entries");
+  c10::cuda::CUDAGuard guard(q.device());
+  at::Tensor out = out_stride.empty() ? at::empty(q.sizes(), q.options())
+                                      : at::empty_strided(q.sizes(), out_stride, q.options());
+  B200kAttentionArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.batch = q.size(0);
+  a.heads = q.size(1);
+  a.kv_heads = k.size(1);
+  a.q_len = q.size(2);
+  a.kv_len = k.size(2);
+  a.head_dim = q.size(3);
+  const at::Tensor* ts[4] = {&q, &k, &v, &out};
+  int64_t* st[4] = {a.q_strides, a.k_strides, a.v_strides, a.out_strides};
+  for (int i = 0; i < 4; ++i)
+    for (int d = 0; d < 4; ++d) st[i][d] = ts[i]->stride(d);
+  a.q = q.data_ptr();
+  a.k = k.data_ptr();
+  a.v = v.data_ptr();
+  a.out = out.data_ptr();
+  a.dtype = to_dt(q.scalar_type());
+  a.causal = causal ? 1 : 0;
+  a.scale = static_cast<float>(scale);
+  a.status = status_word(q.device().index()).data_ptr<int32_t>();
+  check(b200k_attention(&a, stream_of(q)), "attention");
+  return out;
+}
+
 }  // namespace
 
 TORCH_LIBRARY(b200, m) {
@@ -467,6 +506,7 @@ TORCH_LIBRARY(b200, m) {
   m.def("softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("log_softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("rope(Tensor x, Tensor cos, Tensor sin, int[] out_stride=[]) -> Tensor");
+  m.def("attention(Tensor q, Tensor k, Tensor v, bool causal, float scale, int[] out_stride=[]) -> Tensor");
   m.def("gemm_status(int device, bool reset) -> int", &gemm_status);
   m.def("status_check(int device, bool arm) -> int", &status_check);
   m.def("gemm_test_stall_next(int timeout_ns) -> ()", &gemm_test_stall_next);
@@ -481,5 +521,6 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("softmax", &softmax);
   m.impl("log_softmax", &log_softmax);
   m.impl("rope", &rope);
+  m.impl("attention", &attention);
 }
 
