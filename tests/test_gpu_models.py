@@ -54,7 +54,18 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
 
 
-def test_vit_block_stack_bf16():
+@pytest.fixture
+def attention_pass():
+    """The attention pass is opt-in; these tests run it."""
+    from compiler.optimization import config
+
+    old = config.ENABLE_ATTENTION
+    config.ENABLE_ATTENTION = True
+    yield
+    config.ENABLE_ATTENTION = old
+
+
+def test_vit_block_stack_bf16(attention_pass):
     torch.manual_seed(0)
     model = bm.ViT(depth=2).to(DEV, torch.bfloat16).eval()
     x = torch.randn(2, 3, 224, 224, device=DEV, dtype=torch.bfloat16)
@@ -74,7 +85,7 @@ def test_vit_block_stack_bf16():
     assert _rel(got, want) < 2e-2
 
 
-def test_llama_small_bf16():
+def test_llama_small_bf16(attention_pass):
     torch.manual_seed(0)
     model = bm.Llama(vocab=1024, dim=256, layers=2, heads=4, kv_heads=2, ffn=512, max_seq=128)
     bm.init_normal_(model, 0.02, torch.Generator().manual_seed(0))

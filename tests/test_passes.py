@@ -507,7 +507,17 @@ def test_attention_pass_rewrites_sdpa_nodes():
     b200.attention nodes (causal flag, default scale, the replaced node's
     output layout); head_dim other than 64 stays in ATen."""
     import bench_models as bm
+    from compiler.optimization import config
 
+    old = config.ENABLE_ATTENTION
+    config.ENABLE_ATTENTION = True
+    try:
+        _attention_pass_checks(bm)
+    finally:
+        config.ENABLE_ATTENTION = old
+
+
+def _attention_pass_checks(bm):
     torch.manual_seed(0)
     vit = bm.ViT(depth=1).to(torch.bfloat16).eval()
     (g,) = fused_graphs(vit, [torch.randn(2, 3, 224, 224).to(torch.bfloat16)])

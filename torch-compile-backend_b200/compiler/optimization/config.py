@@ -9,7 +9,8 @@ Environment flags (read once at import, overridable as module attributes):
   B200_ROWREDUCE=0    skip the row-reduction pass
   B200_ROPE=0         skip the rotary-embedding pass
   B200_PATCHIFY=0     keep patch-embedding convolutions as convolutions
-  B200_ATTENTION=0    keep ATen's scaled-dot-product attention nodes
+  B200_ATTENTION=1    replace ATen's scaled-dot-product attention nodes with
+                      the library's attention kernel (off by default)
   B200_DUMP=1         print each compiled graph and the fused-kernel programs
   B200_FAST_EPILOGUE=0  always interpret GEMM epilogue programs
   B200_CUDA_GRAPHS=0  run compiled inference graphs op by op instead of
@@ -43,7 +44,10 @@ ENABLE_POINTWISE = _flag("B200_POINTWISE", True)
 ENABLE_ROWREDUCE = _flag("B200_ROWREDUCE", True)
 ENABLE_ROPE = _flag("B200_ROPE", True)
 ENABLE_PATCHIFY = _flag("B200_PATCHIFY", True)
-ENABLE_ATTENTION = _flag("B200_ATTENTION", True)
+# The attention kernel is parity-tested but measured slower than PyTorch's
+# cuDNN SDPA on B200 (Llama-style prefill 327 vs 208 us, ViT-B/16 57 vs 35
+# us per layer), so the pass is opt-in.
+ENABLE_ATTENTION = _flag("B200_ATTENTION", False)
 DUMP = _flag("B200_DUMP", False)
 FAST_EPILOGUE = _flag("B200_FAST_EPILOGUE", True)  # compiled path for canonical GEMM epilogues
 CUDA_GRAPHS = _flag("B200_CUDA_GRAPHS", True)  # replay compiled inference graphs as CUDA graphs

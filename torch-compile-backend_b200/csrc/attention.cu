@@ -11,9 +11,10 @@
 // One CTA per (batch, head, 256 query rows), 384 threads:
 //   warp 0      TMA producer: the CTA's two 128-row query tiles once, then
 //               128-row key and value blocks into a kStages-deep ring;
-//   warp 1      MMA issuer (one thread): S_t = Q_t K^T into tensor memory
-//               (tcgen05.mma M=128, N=128, K=64) and O_t += P_t V
-//               (M=128, N=64, K=128, V read N-major from its TMA tile);
+//   warps 1, 3  MMA issuers (one thread each, for query tile 0 and 1):
+//               S_t = Q_t K^T into tensor memory (tcgen05.mma M=128, N=128,
+//               K=64) and O_t += P_t V (M=128, N=64, K=128, V read N-major
+//               from its TMA tile);
 //   warp 2      owns the tensor-memory allocation (S of both tiles, O of
 //               both tiles: 384 of 512 columns);
 //   warps 4-7   softmax of query tile 0, warps 8-11 of tile 1: one thread per
@@ -62,6 +63,17 @@ static_assert(kSmem <= 232448, "shared memory budget");
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemO = 256;            // O of tile t at column 256 + 64 t
 constexpr float kRescaleLog2 = 8.0f;        // lazy rescale threshold (a factor of 256)
+// Register split (setmaxnreg): the kernel is compiled for kLaunchRegs per
+// thread (384 threads: 64512 registers); the control warpgroup (warps 0-3)
+// drops to kCtlRegs and each softmax warpgroup rises to kSoftmaxRegs (a
+// softmax thread holds its row's 128 scores), which needs
+// 2 x 128 x (200 - 168) = 8192 of the 128 x (168 - 104) = 8192 the control
+// warpgroup returns.  The host launches only when the compiled register
+// count is kLaunchRegs (cudaFuncGetAttributes).
+constexpr int kLaunchRegs = 168;
+constexpr int kCtlRegs = 104;
+constexpr int kSoftmaxRegs = 200;
+static_assert(128 * kCtlRegs + 256 * kSoftmaxRegs <= kThreads * kLaunchRegs, "register split exceeds the launch");
 constexpr float kLog2e = 1.4426950408889634f;
 
 struct Params {
@@ -100,6 +112,15 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <int N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool half) {
   uint32_t u;
@@ -176,8 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* p_full = s_free + 2;
   uint64_t* o_done = p_full + 2;
   uint64_t* o_free = o_done + 2;
-  uint64_t* drain = o_free + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = o_free + 2;  // [2] by MMA thread
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -189,11 +210,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < 2; ++i) {
       gemm::mbar_init(&q_full[i], 1);
-      gemm::mbar_init(&q_empty[i], 1);
+      gemm::mbar_init(&q_empty[i], 2);  // both tiles' MMA threads
     }
     for (int s = 0; s < kStages; ++s) {
       gemm::mbar_init(&kv_full[s], 1);
-      gemm::mbar_init(&kv_empty[s], 1);
+      gemm::mbar_init(&kv_empty[s], 2);
     }
     for (int t = 0; t < 2; ++t) {
       gemm::mbar_init(&s_full[t], 1);
@@ -202,7 +223,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       gemm::mbar_init(&o_done[t], 1);
       gemm::mbar_init(&o_free[t], 4);
     }
-    gemm::mbar_init(drain, 1);
+    gemm::mbar_init(&drain[0], 1);
+    gemm::mbar_init(&drain[1], 1);
     *abort_flag = 0;
     gemm::fence_mbar_init();
   }
@@ -215,7 +237,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   gemm::tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const Ctl ctl{abort_flag, p.status, static_cast<uint64_t>(p.timeout_ns)};
-
+  if (warp < 4) {
+  regs_dec<kCtlRegs>();
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (lane == 0) {
@@ -256,16 +279,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         gemm::wait_bar_drain(&kv_full[k % kStages], static_cast<uint32_t>(k / kStages) & 1u, 100000000ull);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp == 1 || warp == 3) {
+    // ---------------------------------------------------------------- MMA issuers
+    // One thread per query tile (warp 1: tile 0, warp 3: tile 1), so each
+    // tile's products follow its own softmax and neither waits for the
+    // other's.  Each thread's tcgen05.commit tracks only its own MMAs; the
+    // K/V and Q buffers are released when both tiles' threads have arrived.
     if (lane == 0) {
+      const int t = warp == 1 ? 0 : 1;
       bool ok = true;
-      int kv_ready = -1;             // highest K/V block (over all items) waited for
-      int q_ready = -1;              // highest item whose query tiles were waited for
-      int gs[2] = {0, 0};            // score blocks issued per query tile, over all items
-      int gp[2] = {0, 0};            // P V products issued per query tile
-      int items_t[2] = {0, 0};       // items finished per query tile
-      bool s0_ready[2] = {false, false};  // block 0 of the current item's scores issued
+      int kv_ready = -1;  // highest K/V block (over all items) waited for
+      int q_ready = -1;   // highest item whose query tiles were waited for
+      int gs = 0;         // score blocks issued for this tile, over all items
+      int gp = 0;         // P V products issued
+      int items_done = 0; // items whose last product was issued
+      bool s0_ready = false;  // block 0 of the current item's scores issued
       auto ensure_kv = [&](int g) -> bool {
         while (kv_ready < g) {
           ++kv_ready;
@@ -281,10 +309,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         return true;
       };
-      // Scores of query tile t of item li against K/V block g (over all items).
-      auto issue_s = [&](int t, int li, int g) -> bool {
+      // Scores of this tile of item li against K/V block g (over all items).
+      auto issue_s = [&](int li, int g) -> bool {
         if (!ensure_q(li) || !ensure_kv(g)) return false;
-        if (gs[t] > 0 && !gemm::wait_bar(&s_free[t], static_cast<uint32_t>(gs[t] - 1) & 1u, ctl)) return false;
+        if (gs > 0 && !gemm::wait_bar(&s_free[t], static_cast<uint32_t>(gs - 1) & 1u, ctl)) return false;
         gemm::tc_fence_after();
         const uint32_t a0 = smem_u32(sQ + (li & 1) * 2 * kTileBytes + t * kTileBytes);
         const uint32_t b0 = smem_u32(sK + (g % kStages) * kTileBytes);
@@ -292,72 +320,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = 0; k < kD / gemm::UMMA_K; ++k)
           gemm::umma_f16(tmem_base + static_cast<uint32_t>(t * kBKV), gemm::sw128_desc(a0 + k * 32, 16, 1024),
                          gemm::sw128_desc(b0 + k * 32, 16, 1024), p.idesc_s, k != 0 ? 1u : 0u);
-        if (!(t == 0 && gs[t] == 0 && (p.test_flags & B200K_ATTN_TEST_WITHHOLD_SCORES)))
-          gemm::umma_commit(&s_full[t]);
-        ++gs[t];
+        if (!(t == 0 && gs == 0 && (p.test_flags & B200K_ATTN_TEST_WITHHOLD_SCORES))) gemm::umma_commit(&s_full[t]);
+        ++gs;
         return true;
       };
       int kvbase = 0;  // index of the current item's block 0 among all K/V blocks
       int li = 0;
       for (int w = first; w < n_items && ok; w += step, ++li) {
         const Item it = item_at(w, p);
+        const int n = t ? it.n[1] : it.n[0];
         const bool has_next = w + step < n_items;
-        Item nx;
-        if (has_next) nx = item_at(w + step, p);
+        int n_next = 0;
+        if (has_next) {
+          const Item nx = item_at(w + step, p);
+          n_next = t ? nx.n[1] : nx.n[0];
+        }
         const int kvnext = kvbase + it.n_all;
-        bool s0_next[2] = {false, false};
-        for (int t = 0; t < 2 && ok; ++t)
-          if (it.n[t] > 0 && !s0_ready[t]) ok = issue_s(t, li, kvbase);
+        bool s0_next = false;
+        if (n > 0 && !s0_ready) ok = issue_s(li, kvbase);
         for (int j = 0; j < it.n_all && ok; ++j) {
-          for (int t = 0; t < 2 && ok; ++t) {
-            if (j + 1 < it.n[t]) {
-              ok = issue_s(t, li, kvbase + j + 1);
-            } else if (j + 1 == it.n[t] && has_next && nx.n[t] > 0 && kvnext - kStages <= kvbase + j - 1) {
-              // the next item's first scores, while this item finishes (its
-              // first K/V block can already be in the ring)
-              ok = issue_s(t, li + 1, kvnext);
-              s0_next[t] = ok;
+          if (j < n) {
+            // the next scores: block j + 1, or the next item's block 0 while
+            // this item finishes (once that block's ring slot is free)
+            if (j + 1 < n) {
+              ok = issue_s(li, kvbase + j + 1);
+            } else if (has_next && n_next > 0 && kvnext - kStages <= kvbase + j - 1) {
+              ok = issue_s(li + 1, kvnext);
+              s0_next = ok;
             }
             if (!ok) break;
-            if (j < it.n[t]) {
-              // O of the previous item has been read out before the first
-              // product of this one overwrites it
-              if (j == 0 && items_t[t] > 0 &&
-                  !gemm::wait_bar(&o_free[t], static_cast<uint32_t>(items_t[t] - 1) & 1u, ctl)) {
-                ok = false;
-                break;
-              }
-              if (!gemm::wait_bar(&p_full[t], static_cast<uint32_t>(gp[t]) & 1u, ctl)) {
-                ok = false;
-                break;
-              }
-              gemm::tc_fence_after();
-              const uint32_t a0 = smem_u32(sP + t * kPBytes);
-              const uint32_t b0 = smem_u32(sV + ((kvbase + j) % kStages) * kTileBytes);
-#pragma unroll
-              for (int k = 0; k < kBKV / gemm::UMMA_K; ++k)
-                gemm::umma_f16(tmem_base + kTmemO + static_cast<uint32_t>(t * kD),
-                               gemm::sw128_desc(a0 + (k >> 2) * (kBQ * 128) + (k & 3) * 32, 16, 1024),
-                               gemm::sw128_desc(b0 + k * (gemm::UMMA_K * 128), kTileBytes, 1024), p.idesc_pv,
-                               (j | k) != 0 ? 1u : 0u);
-              gemm::umma_commit(&o_done[t]);
-              ++gp[t];
-              if (j + 1 == it.n[t]) ++items_t[t];
+            // O of the previous item has been read out before the first
+            // product of this one overwrites it
+            if (j == 0 && items_done > 0 &&
+                !gemm::wait_bar(&o_free[t], static_cast<uint32_t>(items_done - 1) & 1u, ctl)) {
+              ok = false;
+              break;
             }
+            if (!gemm::wait_bar(&p_full[t], static_cast<uint32_t>(gp) & 1u, ctl)) {
+              ok = false;
+              break;
+            }
+            gemm::tc_fence_after();
+            const uint32_t a0 = smem_u32(sP + t * kPBytes);
+            const uint32_t b0 = smem_u32(sV + ((kvbase + j) % kStages) * kTileBytes);
+#pragma unroll
+            for (int k = 0; k < kBKV / gemm::UMMA_K; ++k)
+              gemm::umma_f16(tmem_base + kTmemO + static_cast<uint32_t>(t * kD),
+                             gemm::sw128_desc(a0 + (k >> 2) * (kBQ * 128) + (k & 3) * 32, 16, 1024),
+                             gemm::sw128_desc(b0 + k * (gemm::UMMA_K * 128), kTileBytes, 1024), p.idesc_pv,
+                             (j | k) != 0 ? 1u : 0u);
+            gemm::umma_commit(&o_done[t]);
+            ++gp;
+            if (j + 1 == n) ++items_done;
+            gemm::umma_commit(&kv_empty[(kvbase + j) % kStages]);  // this tile's reads of block j
+          } else {
+            // This tile does not read block j.  Its arrival waits for the
+            // block's load, so that it can never complete a later phase of
+            // the slot's barrier while the other tile still reads this one.
+            ok = ensure_kv(kvbase + j);
+            if (!ok) break;
+            gemm::mbar_arrive(&kv_empty[(kvbase + j) % kStages]);
           }
-          if (ok) gemm::umma_commit(&kv_empty[(kvbase + j) % kStages]);  // every MMA reading block j is issued
         }
-        if (ok) gemm::umma_commit(&q_empty[li & 1]);  // every score product of this item is issued
-        s0_ready[0] = s0_next[0];
-        s0_ready[1] = s0_next[1];
+        if (!ok) break;
+        if (n > 0) {
+          gemm::umma_commit(&q_empty[li & 1]);  // this tile's score products of item li
+        } else {
+          if (!ensure_q(li)) break;  // (as above: never ahead of the buffer's current phase)
+          gemm::mbar_arrive(&q_empty[li & 1]);
+        }
+        s0_ready = s0_next;
         kvbase = kvnext;
       }
       // Every MMA this thread issued completes before tensor memory is freed.
-      gemm::umma_commit(drain);
-      gemm::wait_bar_drain(drain, 0, 100000000ull);
+      gemm::umma_commit(&drain[t]);
+      gemm::wait_bar_drain(&drain[t], 0, 100000000ull);
     }
     __syncwarp();
-  } else if (warp >= 4) {
+  }
+  } else {
+    regs_inc<kSoftmaxRegs>();
     // ---------------------------------------------------------------- softmax
     const int t = (warp - 4) >> 2;
     const int quarter = warp & 3;
@@ -369,9 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int w = first; w < n_items && ok; w += step) {
       const Item it = item_at(w, p);
-      const int n = it.n[t];
+      const int n = t ? it.n[1] : it.n[0];
       if (n == 0) continue;
-      const int row = it.q0[t] + r;
+      const int q0t = t ? it.q0[1] : it.q0[0];
+      const int row = q0t + r;
       float m = 0.0f, l = 0.0f;  // running max (log2 domain, scaled) and sum
       for (int j = 0; j < n; ++j, ++g) {
         if (!warp_wait(&s_full[t], static_cast<uint32_t>(g) & 1u, ctl)) {
@@ -394,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
         if (lane == 0) gemm::mbar_arrive(&s_free[t]);
         const int col0 = j * kBKV;
-        if (col0 + kBKV > p.Skv || (p.causal && col0 + kBKV - 1 > it.q0[t])) {  // warp-uniform
+        if (col0 + kBKV > p.Skv || (p.causal && col0 + kBKV - 1 > q0t)) {  // warp-uniform
           const int lim = (p.causal ? min(p.Skv - 1, row) : p.Skv - 1) - col0;
 #pragma unroll
           for (int c = 0; c < kBKV; ++c)
@@ -415,16 +458,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           m = mrow;
           resc = true;
         }
-        float sum[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        float2 sum2[2] = {make_float2(0.0f, 0.0f), make_float2(0.0f, 0.0f)};
+        const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), nm2 = make_float2(-m, -m);
 #pragma unroll
         for (int c = 0; c < kBKV; c += 4)
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const float e = gemm::approx_exp2(fmaf(s[c + i], p.scale_log2, -m));
-            s[c + i] = e;
-            sum[i] += e;
+          for (int i = 0; i < 2; ++i) {
+            const float2 x = __ffma2_rn(make_float2(s[c + 2 * i], s[c + 2 * i + 1]), sc2, nm2);
+            const float2 e = make_float2(gemm::approx_exp2(x.x), gemm::approx_exp2(x.y));
+            s[c + 2 * i] = e.x;
+            s[c + 2 * i + 1] = e.y;
+            sum2[i] = __fadd2_rn(sum2[i], e);
           }
-        l = fmaf(l, alpha, (sum[0] + sum[1]) + (sum[2] + sum[3]));
+        l = fmaf(l, alpha, (sum2[0].x + sum2[0].y) + (sum2[1].x + sum2[1].y));
         // The previous product P V has read P (and, within the item, written O).
         if (g > 0) {
           if (!warp_wait(&o_done[t], static_cast<uint32_t>(g - 1) & 1u, ctl)) {
@@ -589,6 +635,12 @@ extern "C" int b200k_attention(const B200kAttentionArgs* a, void* stream_) {
 
   static bool attr_set = false;
   if (!attr_set) {
+    // The register split inside the kernel is sized for kLaunchRegs
+    // registers per thread at launch; with any other count setmaxnreg.inc
+    // could wait for registers that do not exist, so do not launch.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, attention_kernel) != cudaSuccess || fa.numRegs != kLaunchRegs)
+      return B200K_ERR_UNSUPPORTED;
     if (cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem) != cudaSuccess)
       return B200K_ERR_LAUNCH;
     attr_set = true;
