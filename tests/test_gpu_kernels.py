@@ -379,13 +379,15 @@ def test_pointwise_empty_is_noop():
 
 # ------------------------------------------------------------- row kernels
 @pytest.mark.parametrize("rows,cols", [(16384, 8192), (37, 64), (5, 4096), (3, 200), (8, 32768), (9, 2048),
-                                       (6, 1536), (5, 3072), (4, 6144)])
+                                       (6, 1536), (5, 3072), (4, 6144), (1000, 512), (3001, 1024), (2999, 2048)])
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
 @pytest.mark.parametrize("flags", [7, 1])
 def test_rms_norm_swiglu(rows, cols, dtype, flags):
     """16-bit rows whose half is a multiple of 8 run the specialised kernel
-    (flags 7: every rounding of the 16-bit graph); the others, and flag sets
-    it does not implement, the generic one."""
+    (flags 7: every rounding of the 16-bit graph) -- with many rows whose
+    half splits into 64, 128 or 256 x 2 vectors, the row-loop kernel that
+    loads one row ahead (odd row counts end a loop mid-pair); the others, and
+    flag sets it does not implement, the generic one."""
     dt = _tdt(dtype)
     g = torch.Generator(device=DEV).manual_seed(0)
     x = torch.randn(rows, cols, device=DEV, generator=g).to(dt)

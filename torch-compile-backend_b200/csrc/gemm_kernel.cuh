@@ -582,6 +582,19 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+// tcgen05.wait::ld that also names the destination registers of the load it
+// waits for, so that no use of them can be scheduled before it.
+__device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;"
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
 // Adds the row-broadcast bias of columns n..n+31 to v (every lane the same
 // 32 values).  A run inside [0, N) of a unit-stride, 16-byte-aligned vector
 // loads as 4 (16-bit) or 8 (f32) 16-byte vectors whose address is the same
@@ -730,9 +743,11 @@ __device__ __forceinline__ void unpack16x8(uint4 u, int dt, float (&x)[8]) {
 // over all 32 values before the next (bias, activation, rounding, operand,
 // packing), so independent values interleave; the dtype choices are
 // warp-uniform branches around whole steps.
+// The sub-chunk's accumulator values arrive in `raw` (loaded from tensor
+// memory by the caller, one sub-chunk ahead of their use).
 template <int BN, int OUT_BYTES, int ACT, int ROW>
-__device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, uint32_t t_col, int row0,
-                                               int n, int s, int lane, uint8_t* sb, const FastOps& use) {
+__device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, const uint32_t (&raw)[32],
+                                               int row0, int n, int s, int lane, uint8_t* sb, const FastOps& use) {
   constexpr int kEC = 128 / OUT_BYTES;
   constexpr int NSUB = Epi<BN>::CW / 32;
   constexpr int SUB_PER_STG = kEC / 32;
@@ -740,18 +755,9 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
   constexpr bool kMul = ROW == ROW_SCALE || ROW == ROW_SCALE_PK;
   static_assert(OUT_BYTES == 2 || ROW == ROW_NONE, "full-matrix operands are 16-bit, as is the output");
   float v[32];
-  {
-    uint32_t raw[32];
-    tmem_ld32(t_col, raw);
-    tmem_wait_ld();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-  }
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
   const int sub = s % SUB_PER_STG;
-  if (sub == 0) {
-    if (lane == 0) bulk_wait_read_all();
-    __syncwarp();
-  }
   if (p.f_bias >= 0) add_bias32(p, n, v);
 #pragma unroll
   for (int g = 0; g < 4; ++g) apply_act8<ACT>(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
@@ -800,6 +806,12 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
         for (int g = 0; g < 4; ++g) u[g] = pack_f16x8(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
       }
     }
+  }
+  // The staging row is rewritten only once the previous TMA store has read
+  // it; waiting here rather than before the math lets that read overlap it.
+  if (sub == 0) {
+    if (lane == 0) bulk_wait_read_all();
+    __syncwarp();
   }
   if constexpr (OUT_BYTES == 2) {
 #pragma unroll
@@ -888,6 +900,13 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       const int n0 = tn * TN + h * BN + cg * CW;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>((WIDE ? h : acc) * BN + cg * CW);
+      // With 168 registers a thread (up to 384 threads), accumulator columns
+      // are read one sub-chunk ahead: the load of sub-chunk s + 1 is in
+      // flight while sub-chunk s is computed.  The twelve-warp 192-wide
+      // tiles (128 registers a thread) load each sub-chunk when it is due.
+      constexpr bool kAhead = Epi<BN>::kThreads <= 384;
+      uint32_t ahead[32];
+      if (kAhead && n0 < p.N) tmem_ld32(t_row, ahead);
 #pragma unroll 1
       for (int s = 0; s < NSUB; ++s) {
         const int n = n0 + s * 32;
@@ -895,8 +914,19 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
         if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, nxt);
         else if (h + 1 < H) fast_prefetch<ROW>(p, m, n0 + BN, nxt);
         else if (more) fast_prefetch<ROW>(p, m2, n2, nxt);
-        if (n < p.N)  // warp-uniform
-          fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, t_row + s * 32, row0, n, s, lane, sb, cur);
+        if (n < p.N) {  // warp-uniform
+          uint32_t now[32];
+          if constexpr (kAhead) {
+            tmem_wait_ld_regs(ahead);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) now[j] = ahead[j];
+            if (s + 1 < NSUB && n + 32 < p.N) tmem_ld32(t_row + (s + 1) * 32, ahead);
+          } else {
+            tmem_ld32(t_row + s * 32, now);
+            tmem_wait_ld_regs(now);
+          }
+          fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, now, row0, n, s, lane, sb, cur);
+        }
         if (stamper && ti == 0 && h == 0 && s < 4) stamp(p, 249 + 2 * s);
         if constexpr (ROW != ROW_NONE) cur = nxt;
       }

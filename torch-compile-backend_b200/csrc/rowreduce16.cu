@@ -22,6 +22,8 @@
 //     taken on packed bf16x2 / f16x2 pairs: the exact product of two 8- or
 //     11-bit significands fits fp32, so one packed rounding equals fp32
 //     multiply then rounding, bit for bit.
+#include <algorithm>
+
 #include "common.cuh"
 #include "host_common.h"
 #include "rowreduce.cuh"
@@ -358,6 +360,114 @@ __global__ void __launch_bounds__(kRowThreads, min_ctas<2 * VPT>()) swiglu16_ker
 
 #undef B200K_ROW_BEGIN
 
+// ---------------------------------------------------------------------------
+// The same RMSNorm -> split -> silu(gate) * up as swiglu16_kernel, over rows
+// that a row group walks in a grid-stride loop with its loads one row
+// ahead: the gate / up vectors of row r + stride are in flight while row r
+// is reduced, computed and stored, so the memory pipe is not idle while the
+// row's math runs (the one-row-per-group kernel issues every load of a row
+// before any work and nothing during the work; two such CTAs an SM left
+// HBM at 57 % busy).  Two vectors a segment keep both rows' registers
+// (4 x 2 x 4) small enough for three 256-thread CTAs an SM.
+// ---------------------------------------------------------------------------
+template <int TPR, int VPT, bool BF16, bool FULL>
+__global__ void __launch_bounds__(kRowThreads, 3) swiglu16_rows_kernel(const __grid_constant__ RowParams p) {
+  using H = P16<BF16>;
+  constexpr int RPB = kRowThreads / TPR;
+  __shared__ float slots[RPB * 2 * (TPR / 32 > 0 ? TPR / 32 : 1)];
+  const int grp = threadIdx.x / TPR;
+  const int t = threadIdx.x % TPR;
+  const int64_t half = p.cols / 2;
+  const int nvec = static_cast<int>(half / 8);
+  const uint4* w = reinterpret_cast<const uint4*>(p.w);
+  const uint4* wu = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.w) + half);
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * RPB;
+  int64_t row = static_cast<int64_t>(blockIdx.x) * RPB + grp;
+  if (row >= p.rows) return;  // the whole row group leaves together
+  auto load = [&](int64_t r, uint4 (&g)[VPT], uint4 (&u)[VPT]) {
+    const uint16_t* xr = reinterpret_cast<const uint16_t*>(p.x) + r * p.x_stride;
+    load_row<TPR, VPT, FULL>(xr, t, nvec, 0u, g);
+    load_row<TPR, VPT, FULL>(xr + half, t, nvec, 0u, u);
+  };
+  auto process = [&](int64_t r, const uint4 (&g)[VPT], const uint4 (&u)[VPT], int parity) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = H::lo(word(g[k], i)), b = H::hi(word(g[k], i));
+        const float c = H::lo(word(u[k], i)), d = H::hi(word(u[k], i));
+        s = fmaf(a, a, s);
+        s = fmaf(b, b, s);
+        s = fmaf(c, c, s);
+        s = fmaf(d, d, s);
+      }
+    }
+    s = group_reduce<TPR, false>(s, slots, grp, parity);
+    const float rstd = rsqrtf(s / static_cast<float>(p.cols) + p.eps);
+    if (t == 0 && p.rstd_out) p.rstd_out[r] = rstd;
+    uint4* out = reinterpret_cast<uint4*>(reinterpret_cast<uint16_t*>(p.out) + r * p.out_stride);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      const int vi = t + k * TPR;
+      const bool ok = FULL || vi < nvec;
+      const int vc = ok ? vi : 0;
+      const uint4 wgv = __ldg(w + vc), wuv = __ldg(wu + vc);
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t gw = word(g[k], i), uw = word(u[k], i);
+        const uint32_t yg = H::mul(H::pack(H::lo(gw) * rstd, H::hi(gw) * rstd), word(wgv, i));
+        const uint32_t yu = H::mul(H::pack(H::lo(uw) * rstd, H::hi(uw) * rstd), word(wuv, i));
+        const float ga = H::lo(yg), gb = H::hi(yg);
+        const uint32_t sg = H::pack(__fmul_rn(ga, op_sigmoid(ga)), __fmul_rn(gb, op_sigmoid(gb)));
+        o[i] = H::mul(sg, yu);
+      }
+      if (ok) out[vi] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  };
+  uint4 g0[VPT], u0[VPT], g1[VPT], u1[VPT];
+  load(row, g0, u0);
+  int parity = 0;
+  for (;;) {
+    const int64_t r1 = row + stride;
+    if (r1 < p.rows) load(r1, g1, u1);
+    process(row, g0, u0, parity);
+    parity ^= 1;
+    if (r1 >= p.rows) break;
+    const int64_t r2 = r1 + stride;
+    if (r2 < p.rows) load(r2, g0, u0);
+    process(r1, g1, u1, parity);
+    parity ^= 1;
+    if (r2 >= p.rows) break;
+    row = r2;
+  }
+}
+
+// Launches swiglu16_rows_kernel when a segment of the row splits into
+// TPR x 2 vectors with TPR in {64, 128, 256}; -1 otherwise.
+int launch_swiglu_rows(bool bf16, const RowParams& p, int64_t nvec, cudaStream_t st) {
+  int tpr = 0;
+  const int vpt = 2;
+  for (int tt : {64, 128, 256})
+    if (static_cast<int64_t>(tt) * vpt == nvec) tpr = tt;
+  if (!tpr) return -1;
+  const int rpb = kRowThreads / tpr;
+  const int sms = device_sm_count();
+  if (sms <= 0) return B200K_ERR_DEVICE;
+  const int64_t groups = (p.rows + rpb - 1) / rpb;
+  const int grid = static_cast<int>(std::min<int64_t>(groups, 3 * static_cast<int64_t>(sms)));
+#define B200K_SWR(T, V)                                                                                  \
+  if (tpr == T && vpt == V) {                                                                            \
+    if (bf16) swiglu16_rows_kernel<T, V, true, true><<<grid, kRowThreads, 0, st>>>(p);                   \
+    else swiglu16_rows_kernel<T, V, false, true><<<grid, kRowThreads, 0, st>>>(p);                       \
+    return cudaGetLastError() == cudaSuccess ? B200K_OK : B200K_ERR_LAUNCH;                              \
+  }
+  B200K_SWR(64, 2) B200K_SWR(128, 2) B200K_SWR(256, 2)
+#undef B200K_SWR
+  return -1;
+}
+
 // (TPR, VPT) for a row of nvec 16-byte vectors per segment: the fewest
 // threads per row (a warp if it can), then the fewest vectors per thread,
 // at most 16 vectors per thread over all segments; false past 256 threads
@@ -444,7 +554,14 @@ int launch_row16(Row16Kind kind, const RowParams& p, cudaStream_t st) {
     case R16_LAYERNORM:
       return p.flags == 0 ? launch_tv<KLayer>(tpr, vpt, bf16, p, span / 8, st) : -1;
     case R16_SWIGLU:
-      if (p.flags == (kNormed | kAffine | kSilu) && p.w) return launch_tv<KSwiglu>(tpr, vpt, bf16, p, span / 8, st);
+      if (p.flags == (kNormed | kAffine | kSilu) && p.w) {
+        // rows long enough for the pipelined row loop take it
+        if (p.rows >= 4 * static_cast<int64_t>(device_sm_count())) {
+          const int rc = launch_swiglu_rows(bf16, p, span / 8, st);
+          if (rc != -1) return rc;
+        }
+        return launch_tv<KSwiglu>(tpr, vpt, bf16, p, span / 8, st);
+      }
       return -1;
   }
   return -1;
