@@ -408,6 +408,66 @@ def run_sweep(args, dist: Dist) -> dict:
     }
 
 
+def run_sweep_backend(args, dist: Dist) -> dict:
+    """The sweep through torch.compile with another backend (the reference
+    Triton backend from baseline/_ref, eager, or inductor), inputs resident
+    on the device: each block's call timed with CUDA events, an L2 flush
+    between steps, value = sweep FLOPs / summed device time.  The blocks are
+    the default workload's (same shapes, seeds and epilogues)."""
+    from bench_models import GemmEpilogueBlock, init_sweep_block
+
+    be = _backend(args.backend)
+    dev = torch.device("cuda", dist.local)
+    torch.cuda.set_device(dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    torch._dynamo.config.recompile_limit = max(torch._dynamo.config.recompile_limit, 64)
+    flush = torch.empty(2 * L2_BYTES // 4, dtype=torch.float32, device=dev)
+    calls, flops = [], 0.0
+    t0 = time.perf_counter()
+    for (M, N, K) in SWEEP:
+        x = (0.02 * torch.randn(M, K, device=dev, generator=gen)).to(torch.bfloat16)
+        r = (0.02 * torch.randn(M, N, device=dev, generator=gen)).to(torch.bfloat16)
+        for act in ACTS:
+            blk = GemmEpilogueBlock(K, N, act)
+            init_sweep_block(blk, torch.Generator().manual_seed(len(calls)))
+            blk = blk.to(dev, torch.bfloat16).eval()
+            f = blk if be is None else torch.compile(blk, backend=be)
+            calls.append((f, x, r))
+            flops += 2.0 * M * N * K
+    with torch.no_grad():
+        for f, x, r in calls:  # compile (and, for the reference, autotune) each block
+            f(x, r)
+        torch.cuda.synchronize()
+        compile_s = time.perf_counter() - t0
+        per = [_time_device(lambda f=f, x=x, r=r: f(x, r), args.steps, args.warmup, flush) for f, x, r in calls]
+    total_ms = sum(statistics.median(t) for t in per)
+    return {"metric": "fused GEMM+epilogue TFLOP/s", "value": round(flops / (total_ms * 1e-3) / 1e12, 2),
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(total_ms, 4), "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "gemm_epilogue_sweep", "backend": args.backend},
+            "compile_s": round(compile_s, 1)}
+
+
+def _reference_triton_sweep(steps: int, warmup: int) -> dict:
+    """run_sweep_backend with the reference Triton backend, in a process of
+    its own (its package is also named `compiler`)."""
+    cmd = [sys.executable, os.path.join(ROOT, "bench.py"), "--workload", "sweep", "--backend", "reference_triton",
+           "--steps", str(steps), "--warmup", str(warmup)]
+    env = dict(os.environ)
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE", "MASTER_ADDR", "MASTER_PORT"):
+        env.pop(k, None)
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=900, env=env)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "timed out after 900 s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode == 0 and lines:
+        d = json.loads(lines[-1])
+        return {"value": d["value"], "unit": d["unit"], "ms": d["ms_per_step"], "compile_s": d["compile_s"]}
+    err = [ln for ln in r.stderr.splitlines() if "Error" in ln or "error" in ln]
+    return {"unavailable": (err[-1] if err else f"exit code {r.returncode}")[:300]}
+
+
 def run_single_gemm(args, dist: Dist) -> dict:
     """One sweep point on its own: --shape M,N,K --act none|gelu|silu [--tile-config c].
     Used for ncu captures and for measuring the tile table."""
@@ -882,7 +942,7 @@ def main() -> None:
     ap.add_argument("--workload", default="sweep",
                     choices=["sweep", "gemm", "vit", "llama", "chain", "pointwise", "attention"])
     ap.add_argument("--backend", default="ours", choices=["ours", "eager", "reference_triton", "inductor"],
-                    help="vit/llama/chain workloads: which torch.compile backend runs the model")
+                    help="sweep/vit/llama/chain workloads: which torch.compile backend runs the model")
     ap.add_argument("--batch", type=int, default=0, help="vit/llama batch (default: the benchmark config)")
     ap.add_argument("--shape", default="4096,4096,4096", help="M,N,K for --workload gemm")
     ap.add_argument("--act", default="gelu", choices=ACTS, help="epilogue activation for --workload gemm")
@@ -935,11 +995,16 @@ def main() -> None:
         if args.workload == "attention":
             print(json.dumps(run_attention(args, dist)))
             return
+        if args.backend != "ours":
+            print(json.dumps(run_sweep_backend(args, dist)))
+            return
         res = run_sweep(args, dist)
         res["host_cpus_bound"] = len(cpus) if cpus else None
         if not args.no_extras:
             res["models"] = run_model_extras(args, dist)
             res["chain"] = run_chain_extra(args, dist)
+            if dist.world == 1 and args.reference_models:
+                res["sweep_reference_triton"] = _reference_triton_sweep(args.model_steps, max(3, args.warmup))
         if dist.rank == 0:
             if dist.world == 1 and not args.no_extras:
                 res["cpu_baseline"] = _cpu_baseline_subprocess(args.cpu_rows)
