@@ -552,3 +552,35 @@ def test_gemm_stalled_wait_times_out_and_context_survives(config):
                                 [b.float().cpu().numpy(), r[:64].float().cpu().numpy()], "bfloat16",
                                 bias=b.float().cpu().numpy())
     _assert_close(out[:64], want, *_gemm_tol(want))
+
+
+# ------------------------------------------------------------- TF32
+@pytest.mark.parametrize("M,N,K", [(1000, 520, 300), (512, 1024, 2048), (4096, 4096, 1024)])
+@pytest.mark.parametrize("case", ["gelu", "silu_residual", "bias_to_bf16"])
+@pytest.mark.parametrize("config", [-1, 1])
+def test_gemm_tf32(M, N, K, case, config):
+    """fp32 operands on the TF32 tensor cores (what the backend emits when
+    torch allows TF32): the compiled form (bias + activation, fp32 out), the
+    interpreter (fp32 residual; a cast to bf16) and the 128-wide tile, against
+    the fp32 oracle.  TF32 rounds each operand to 10 significand bits, so the
+    bound is 5e-3 relative to the output's magnitude."""
+    g = torch.Generator(device=DEV).manual_seed(M + N + K)
+    x = torch.randn(M, K, device=DEV, generator=g)
+    w = torch.randn(N, K, device=DEV, generator=g) / K ** 0.5
+    b = 0.1 * torch.randn(N, device=DEV, generator=g)
+    r = torch.randn(M, N, device=DEV, generator=g)
+    act, res, out_dt = {"gelu": ("gelu", False, "float32"), "silu_residual": ("silu", True, "float32"),
+                        "bias_to_bf16": ("none", False, "bfloat16")}[case]
+    code, imm, spec, form = epilogue_program(act, residual=res)
+    out = torch.empty(M, N, device=DEV, dtype=_tdt(out_dt))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    extras = [b, r] if res else [b]
+    cabi.gemm_epilogue(x, w.t(), extras, code, imm, out, tile_config=config, status=status, form=form)
+    torch.cuda.synchronize()
+    assert status.item() == 0
+    rows = slice(0, 96)
+    want = oracle.gemm_epilogue(x[rows].cpu().numpy(), w.cpu().numpy().T, spec,
+                                [b.cpu().numpy()] + ([r[rows].cpu().numpy()] if res else []), out_dt,
+                                bias=b.cpu().numpy())
+    tol = 5e-3 * float(np.abs(want).max() + 1e-6)
+    _assert_close(out[rows], want, 5e-3 if out_dt == "float32" else 1e-2, tol)

@@ -195,3 +195,28 @@ def test_check_status_raises_after_a_stalled_gemm():
     with pytest.raises(RuntimeError, match="status 6"):
         runtime.check_status()
     runtime.check_status()  # cleared
+
+
+def test_fp32_mlp_fuses_on_tf32_when_allowed():
+    """With torch's allow_tf32 on, the fp32 MLP's two GEMMs take the
+    library's TF32 kernels (bias + tanh-GELU, bias + residual) and match
+    eager cuBLAS TF32; with it off they stay cuBLAS fp32, as in the
+    reference (compiler/optimization/fusion_epilogue.py:82-86)."""
+    import sweep_inputs as si
+
+    m, x = si.mlp()
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        for allow in (True, False):
+            torch.backends.cuda.matmul.allow_tf32 = allow
+            torch._dynamo.reset()
+            be, graphs = capturing_backend()
+            with torch.no_grad():
+                want = m(x)
+                got = torch.compile(m, backend=be)(x)
+            t = [str(s) for s in b200_targets(graphs)]
+            assert t.count("b200.gemm_epilogue.default") == (2 if allow else 0)
+            assert _rel(got, want) < (5e-3 if allow else 1e-5)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    runtime.check_status()

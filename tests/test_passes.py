@@ -535,3 +535,20 @@ def _attention_pass_checks(bm):
     small = bm.Llama(vocab=256, dim=128, layers=1, heads=4, kv_heads=2, ffn=256, max_seq=64).to(torch.bfloat16).eval()
     (g,) = fused_graphs(small, [torch.randint(0, 256, (2, 64))])
     assert not any(n.target == torch.ops.b200.attention.default for n in g.graph.nodes if n.op == "call_function")
+
+
+def test_fp32_epilogue_fusion_follows_allow_tf32():
+    """fp32 GEMMs are fused (TF32 kernels) only while torch allows TF32,
+    the reference's rule for its fp32 dots; otherwise they stay ATen."""
+    model, inputs = make_case("mlp_block_fp32")
+    old = torch.backends.cuda.matmul.allow_tf32
+    try:
+        counts = {}
+        for allow in (True, False):
+            torch.backends.cuda.matmul.allow_tf32 = allow
+            (g,) = fused_graphs(model, inputs)
+            counts[allow] = sum(1 for n in g.graph.nodes if n.op == "call_function"
+                                and n.target == torch.ops.b200.gemm_epilogue.default)
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = old
+    assert counts[True] >= 1 and counts[False] == 0

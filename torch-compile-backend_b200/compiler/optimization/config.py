@@ -63,6 +63,16 @@ LOADABLE_DTYPES = {
 }
 STORABLE_DTYPES = {torch.float32, torch.float16, torch.bfloat16, torch.float64}
 GEMM_AB_DTYPES = {torch.float16, torch.bfloat16}
+
+
+def gemm_ab_dtypes() -> set:
+    """Operand dtypes the GEMM kernels take now: 16-bit always, fp32 when
+    torch allows TF32 for matmuls (the kernels then run TF32 tensor cores,
+    as cuBLAS would; the reference likewise lets its fp32 dots use TF32 only
+    under that flag, compiler/optimization/fusion_epilogue.py:82-86)."""
+    if torch.backends.cuda.matmul.allow_tf32:
+        return GEMM_AB_DTYPES | {torch.float32}
+    return GEMM_AB_DTYPES
 GEMM_OUT_DTYPES = {torch.float16, torch.bfloat16, torch.float32}
 ROW_DTYPES = {torch.float32, torch.float16, torch.bfloat16}
 

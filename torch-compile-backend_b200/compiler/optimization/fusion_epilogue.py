@@ -48,16 +48,17 @@ def _kernel_supports(mat1, mat2, out_meta, extras_meta, out_shape) -> bool:
     mismatch leaves the group to ATen at compile time, as the reference does
     for anything it cannot anchor)."""
     a, b = _tensor_meta(mat1), _tensor_meta(mat2)
-    if a.dtype not in config.GEMM_AB_DTYPES or out_meta.dtype not in config.GEMM_OUT_DTYPES:
+    if a.dtype not in config.gemm_ab_dtypes() or out_meta.dtype not in config.GEMM_OUT_DTYPES:
         return False
     M, K = a.shape
     N = b.shape[1]
     if min(M, N, K) == 0:
         return False
-    if a.stride(1) != 1 or (a.stride(0) * 2) % 16 != 0:
+    eb = a.element_size()
+    if a.stride(1) != 1 or (a.stride(0) * eb) % 16 != 0:
         return False
-    k_major = b.stride(0) == 1 and (b.stride(1) * 2) % 16 == 0
-    n_major = b.stride(1) == 1 and (b.stride(0) * 2) % 16 == 0
+    k_major = b.stride(0) == 1 and (b.stride(1) * eb) % 16 == 0
+    n_major = b.stride(1) == 1 and (b.stride(0) * eb) % 16 == 0 and eb == 2  # TF32 runs K-major B only
     if not (k_major or n_major):
         return False
     if len(extras_meta) > config.MAX_INPUTS - 1:
@@ -204,7 +205,8 @@ def fusion_pays(M: int, N: int, K: int, acc_bytes: int, out_bytes: int, extra_by
     and writes the output.  Fused, the library's GEMM (its time ratio to
     cuBLAS above) applies the group in its epilogue; the extra operands are
     read under the MMAs."""
-    t_mm = 2.0 * M * N * K / GEMM_FLOPS
+    # fp32 operands run at the TF32 rate, half the 16-bit one
+    t_mm = 2.0 * M * N * K / (GEMM_FLOPS / 2 if acc_bytes == 4 else GEMM_FLOPS)
     tail = (2.0 * M * N * acc_bytes + M * N * out_bytes + extra_bytes) / HBM_BYTES + LAUNCH_S
     return library_over_cublas(K) * t_mm <= t_mm + tail
 

@@ -71,9 +71,18 @@ int launch_row16(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CU
 #define B200K_FAST_FN2(BN, ACT) launch_fast_##BN##_##ACT
 #define B200K_FAST_FN(BN, ACT) B200K_FAST_FN2(BN, ACT)
 
-int B200K_FAST_FN(B200K_FAST_BN, B200K_FAST_ACT)(bool bnm, int ob, int row, const CUtensorMap& ta,
+int B200K_FAST_FN(B200K_FAST_BN, B200K_FAST_ACT)(bool tf32, bool bnm, int ob, int row, const CUtensorMap& ta,
                                                  const CUtensorMap& tb, const CUtensorMap& to, const Params& p,
                                                  int grid, cudaStream_t st) {
+  if (tf32) {
+    // fp32 operands (TF32 tensor cores): K-major B, fp32 output, no row
+    // operand -- the compiled forms of an fp32 model's bias + activation
+#if B200K_FAST_BN != 192
+    if (!bnm && ob == 4 && row == ROW_NONE)
+      return launch_one<kBN, kStages, false, 4, true, kAct, ROW_NONE, true>(ta, tb, to, p, grid, st);
+#endif
+    return B200K_ERR_UNSUPPORTED;
+  }
   if (ob == 2) return bnm ? launch_row16<true>(row, ta, tb, to, p, grid, st)
                           : launch_row16<false>(row, ta, tb, to, p, grid, st);
   if (ob == 4 && !bnm && row == ROW_NONE)

@@ -184,6 +184,18 @@ __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// fp32 operands on the tensor cores in TF32 (each operand's significand
+// rounded to 10 bits), fp32 accumulate: the same 32-byte K step as the
+// 16-bit form (8 elements instead of 16).
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
@@ -963,7 +975,10 @@ struct Cfg {
   static_assert(2 * BN <= kTmemCols, "two accumulators fit the allocation");
 };
 
-template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW>
+// TF32: fp32 A and B (K-major B only); a K block is then 32 elements, the
+// same 128 bytes a row as 64 16-bit ones, so the shared-memory layout,
+// descriptors and stage sizes are those of the 16-bit kernel.
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW, bool TF32 = false>
 __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
     gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
@@ -1036,13 +1051,15 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
           if (kb == 0) stamp_tile(p, ti, 0);
           if (kb == p.k_blocks - 1) stamp_tile(p, ti, 1);
           mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
-          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * BK, tm * BM);
+          constexpr int kKb = TF32 ? BK / 2 : BK;  // elements of a K block
+          static_assert(!(TF32 && B_NMAJOR), "TF32 runs K-major B only");
+          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kKb, tm * BM);
           if (B_NMAJOR) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
               tma_load_2d(sB + s * C::kBBytes + j * (64 * BK * 2), &tmB, &full[s], tn * BN + j * 64, kb * BK);
           } else {
-            tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * BK, tn * BN);
+            tma_load_2d(sB + s * C::kBBytes, &tmB, &full[s], kb * kKb, tn * BN);
           }
           ++issued;
           if (++s == STAGES) {
@@ -1087,7 +1104,8 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
             const uint64_t ad = sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024);
             const uint64_t bd = B_NMAJOR ? sw128_desc(b0 + k * (UMMA_K * 128), 64 * BK * 2, 1024)
                                          : sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024);
-            umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+            if constexpr (TF32) umma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
+            else umma_f16(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
           if (kb == max(0, p.k_blocks - kSoonBlocks)) mbar_arrive(&tsoon[acc]);
@@ -1439,11 +1457,11 @@ struct TileConfig {
 constexpr TileConfig kConfigs[] = {{128, 256, 4}, {128, 128, 6}, {128, 192, 4}, {256, 256, 6}, {256, 512, 4}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW>
+template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW, bool TF32 = false>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
                cudaStream_t st) {
   using C = Cfg<BN, STAGES, BNM, OB>;
-  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT, ROW>;
+  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT, ROW, TF32>;
   static bool attr_set = false;  // per instantiation; idempotent
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)
@@ -1463,7 +1481,7 @@ constexpr int kFastActs[] = {B200K_ACT_NONE, B200K_ACT_GELU_ERF, B200K_ACT_GELU_
 // with 16-bit output and every row role, and K-major B with fp32 output
 // without a row operand; B200K_ERR_UNSUPPORTED for anything else.
 #define B200K_DECLARE_FAST(BN, ACT)                                                                          \
-  int launch_fast_##BN##_##ACT(bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb,     \
+  int launch_fast_##BN##_##ACT(bool tf32, bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb, \
                                const CUtensorMap& to, const Params& p, int grid, cudaStream_t st);
 B200K_DECLARE_FAST(256, 0)
 B200K_DECLARE_FAST(256, 1)

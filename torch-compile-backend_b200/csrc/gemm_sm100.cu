@@ -143,8 +143,13 @@ int check_form_cached(const B200kEpilogueForm& f, const B200kProgram& prog, int 
 }
 
 template <int BN, int STAGES>
-int launch_interp(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
+int launch_interp(bool tf32, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
                   const Params& p, int grid, cudaStream_t st) {
+  if (tf32) {  // fp32 operands on TF32 tensor cores, K-major B
+    if (bnm) return B200K_ERR_UNSUPPORTED;
+    return ob == 2 ? launch_one<BN, STAGES, false, 2, false, -1, ROW_NONE, true>(ta, tb, to, p, grid, st)
+                   : launch_one<BN, STAGES, false, 4, false, -1, ROW_NONE, true>(ta, tb, to, p, grid, st);
+  }
   if (bnm) {
     return ob == 2 ? launch_one<BN, STAGES, true, 2, false, -1, ROW_NONE>(ta, tb, to, p, grid, st)
                    : launch_one<BN, STAGES, true, 4, false, -1, ROW_NONE>(ta, tb, to, p, grid, st);
@@ -153,10 +158,10 @@ int launch_interp(bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb
                  : launch_one<BN, STAGES, false, 4, false, -1, ROW_NONE>(ta, tb, to, p, grid, st);
 }
 
-int launch_fast(int bn, int act, bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb,
+int launch_fast(int bn, int act, bool tf32, bool bnm, int ob, int row, const CUtensorMap& ta, const CUtensorMap& tb,
                 const CUtensorMap& to, const Params& p, int grid, cudaStream_t st) {
 #define B200K_FAST_CASE(BN, ACT) \
-  if (bn == BN && act == ACT) return launch_fast_##BN##_##ACT(bnm, ob, row, ta, tb, to, p, grid, st);
+  if (bn == BN && act == ACT) return launch_fast_##BN##_##ACT(tf32, bnm, ob, row, ta, tb, to, p, grid, st);
   B200K_FAST_CASE(256, 0)
   B200K_FAST_CASE(256, 1)
   B200K_FAST_CASE(256, 2)
@@ -279,7 +284,12 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (!a->a || !a->b || !a->out) return B200K_ERR_ARG;
   if (a->K == 0) return B200K_ERR_SHAPE;
   if (a->M > 0x7fffffff || a->N > 0x7fffffff || a->K > 0x7fffffff) return B200K_ERR_SHAPE;
-  if (a->ab_dtype != B200K_BF16 && a->ab_dtype != B200K_F16) return B200K_ERR_UNSUPPORTED;
+  // fp32 operands run on the TF32 tensor cores (the caller passes them only
+  // where TF32 is allowed, as torch's allow_tf32 governs cuBLAS)
+  if (a->ab_dtype != B200K_BF16 && a->ab_dtype != B200K_F16 && a->ab_dtype != B200K_F32)
+    return B200K_ERR_UNSUPPORTED;
+  const bool tf32 = a->ab_dtype == B200K_F32;
+  const int eb = tf32 ? 4 : 2;  // operand element bytes
   if (a->out_dtype != B200K_BF16 && a->out_dtype != B200K_F16 && a->out_dtype != B200K_F32)
     return B200K_ERR_UNSUPPORTED;
   if (a->n_extras < 0 || a->n_extras > B200K_MAX_INPUTS - 1) return B200K_ERR_ARG;
@@ -292,15 +302,15 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
 
   // A: [M, K], unit K stride, rows 16-byte aligned.
   if (a->a_stride_k != 1 && a->K > 1) return B200K_ERR_UNSUPPORTED;
-  if (!aligned16(a->a) || (a->a_stride_m * 2) % 16 != 0) return B200K_ERR_ALIGN;
-  // B: K-major (unit K stride) or N-major (unit N stride).
+  if (!aligned16(a->a) || (a->a_stride_m * eb) % 16 != 0) return B200K_ERR_ALIGN;
+  // B: K-major (unit K stride) or N-major (unit N stride; 16-bit only).
   bool bnm;
   if (a->b_stride_k == 1) {
     bnm = false;
-    if (!aligned16(a->b) || (a->b_stride_n * 2) % 16 != 0) return B200K_ERR_ALIGN;
-  } else if (a->b_stride_n == 1) {
+    if (!aligned16(a->b) || (a->b_stride_n * eb) % 16 != 0) return B200K_ERR_ALIGN;
+  } else if (a->b_stride_n == 1 && !tf32) {
     bnm = true;
-    if (!aligned16(a->b) || (a->b_stride_k * 2) % 16 != 0) return B200K_ERR_ALIGN;
+    if (!aligned16(a->b) || (a->b_stride_k * eb) % 16 != 0) return B200K_ERR_ALIGN;
   } else {
     return B200K_ERR_UNSUPPORTED;
   }
@@ -335,14 +345,14 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
                     (bias_mode == XM_NONE || bias_mode == XM_BCAST);
 
-  const bool pair_ok = fast && !bnm && ob == 2;  // the CTA-pair kernels' domain
+  const bool pair_ok = fast && !bnm && ob == 2 && !tf32;  // the CTA-pair kernels' domain
 
   const int sms = device_sm_count();
   if (sms <= 0) return B200K_ERR_DEVICE;
   int cfg = a->tile_config;
   if (cfg < 0) cfg = pick(a->M, a->N, a->K, sms, fast, pair_ok);
   if (cfg >= kNumConfigs) return B200K_ERR_ARG;
-  if (kConfigs[cfg].bn == 192 && !fast) cfg = 0;  // 192-wide tiles run compiled epilogues only
+  if (kConfigs[cfg].bn == 192 && (!fast || tf32)) cfg = 0;  // 192-wide tiles: compiled 16-bit epilogues only
   if (kConfigs[cfg].bm == 2 * BM && !pair_ok) cfg = 0;
   const int bn = kConfigs[cfg].bn;
   const int bm = kConfigs[cfg].bm;
@@ -360,7 +370,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const int64_t tiles = static_cast<int64_t>(p.tiles_m) * p.tiles_n;
   if (tiles > 0x7fffffff) return B200K_ERR_SHAPE;
   p.num_tiles = static_cast<int32_t>(tiles);
-  p.k_blocks = static_cast<int32_t>((a->K + BK - 1) / BK);
+  const int kb_elems = tf32 ? BK / 2 : BK;  // a K block is 128 bytes of each operand row
+  p.k_blocks = static_cast<int32_t>((a->K + kb_elems - 1) / kb_elems);
   p.n_extras = a->n_extras;
   p.out_dt = a->out_dtype;
   p.out = a->out;
@@ -368,7 +379,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.status = a->status;
   p.timeout_ns = a->timeout_ns > 0 ? a->timeout_ns : 2000000000ll;
   p.test_flags = a->test_flags;
-  const uint32_t fmt = a->ab_dtype == B200K_BF16 ? 1u : 0u;
+  // operand format of the instruction descriptor: f16 0 / bf16 1 (kind::f16), tf32 2 (kind::tf32)
+  const uint32_t fmt = tf32 ? 2u : (a->ab_dtype == B200K_BF16 ? 1u : 0u);
   p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) |
             (static_cast<uint32_t>(mma_n >> 3) << 17) | (static_cast<uint32_t>(bm >> 4) << 24);
   p.group_m = pair ? kGroupMPair : kGroupM;
@@ -405,12 +417,12 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
 
   CUtensorMap ta, tb, to;
   std::memset(&to, 0, sizeof(to));
-  if (!make_map(&ta, a->ab_dtype, a->a, a->K, a->M, a->a_stride_m * 2, BK, BM)) return B200K_ERR_LAUNCH;
+  if (!make_map(&ta, a->ab_dtype, a->a, a->K, a->M, a->a_stride_m * eb, kb_elems, BM)) return B200K_ERR_LAUNCH;
   if (bnm) {
-    if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * 2, 64, BK)) return B200K_ERR_LAUNCH;
+    if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * eb, 64, BK)) return B200K_ERR_LAUNCH;
   } else {
     // a CTA of a pair loads its half of each MMA's B rows
-    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * 2, BK, pair ? kPairMmaN / 2 : bn))
+    if (!make_map(&tb, a->ab_dtype, a->b, a->K, a->N, a->b_stride_n * eb, kb_elems, pair ? kPairMmaN / 2 : bn))
       return B200K_ERR_LAUNCH;
   }
   p.direct_store = tma_out ? 0 : 1;
@@ -435,10 +447,12 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
       p.f_round = -1;  // the store's own rounding is the same one
     }
     if (pair) return launch_pair(wide, a->form.act, row, ta, tb, to, p, grid, st);
-    return launch_fast(bn, a->form.act, bnm, ob, row, ta, tb, to, p, grid, st);
+    const int rc = launch_fast(bn, a->form.act, tf32, bnm, ob, row, ta, tb, to, p, grid, st);
+    if (rc != B200K_ERR_UNSUPPORTED || !tf32) return rc;
+    // TF32 forms without a compiled kernel (a row operand, 16-bit output) interpret the program
   }
-  if (cfg == 0) return launch_interp<256, 4>(bnm, ob, ta, tb, to, p, grid, st);
-  return launch_interp<128, 6>(bnm, ob, ta, tb, to, p, grid, st);
+  if (cfg == 0 || bn == 192) return launch_interp<256, 4>(tf32, bnm, ob, ta, tb, to, p, grid, st);
+  return launch_interp<128, 6>(tf32, bnm, ob, ta, tb, to, p, grid, st);
 }
 
 // ---------------------------------------------------------------------------
