@@ -296,12 +296,15 @@ def run_sweep(args, dist: Dist) -> dict:
     # End to end through torch.compile(custom_backend) with host buffers.
     # The twelve blocks are instances of one class, so dynamo compiles the
     # same frame once per block: its recompile limit (8 by default) would
-    # send the last blocks to eager PyTorch.  Raise it for this run and make
-    # hitting it an error, so every e2e call goes through the backend.
+    # send the last blocks to eager PyTorch, and its automatic dynamic shapes
+    # would compile the blocks after a shape change with symbolic sizes,
+    # which the fusion passes (static shapes) leave to ATen.  Raise the limit
+    # and make hitting it an error, compile with static shapes, and check
+    # below that every block's graph holds a fused GEMM.
     torch._dynamo.reset()
     torch._dynamo.config.recompile_limit = max(torch._dynamo.config.recompile_limit, 4 * len(probs))
     torch._dynamo.config.fail_on_recompile_limit_hit = True
-    compiled = [torch.compile(p["block"], backend=custom_backend) for p in probs]
+    compiled = [torch.compile(p["block"], backend=custom_backend, dynamic=False) for p in probs]
     host = []
     for p in probs:
         M, N, K = p["shape"]
@@ -335,13 +338,14 @@ def run_sweep(args, dist: Dist) -> dict:
 
     from compiler import backend as _backend
 
-    graphs0 = _backend.GRAPHS_COMPILED
+    graphs0, gemms0 = _backend.GRAPHS_COMPILED, _backend.GEMMS_FUSED
     for _ in range(max(1, args.warmup)):
         e2e_step()
     compute.wait_stream(down)
     e2e_graphs = _backend.GRAPHS_COMPILED - graphs0
-    if e2e_graphs < len(probs):
-        raise RuntimeError(f"only {e2e_graphs} of {len(probs)} e2e blocks compiled through the backend")
+    e2e_gemms = _backend.GEMMS_FUSED - gemms0
+    if e2e_graphs < len(probs) or e2e_gemms < len(probs):
+        raise RuntimeError(f"{e2e_graphs} graphs with {e2e_gemms} fused GEMMs for {len(probs)} e2e blocks")
     torch.cuda.synchronize()
     dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -399,7 +403,8 @@ def run_sweep(args, dist: Dist) -> dict:
                                      "capture of this kernel is summarised under profiles/"},
         "e2e": {"value": round(n * flops / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": round(e2e_ms, 3),
-                "graphs_compiled": e2e_graphs},
+                "graphs_compiled": e2e_graphs, "gemms_fused": e2e_gemms,
+                "copy_gbs": round((h2d + d2h) / (e2e_ms * 1e-3) / 1e9, 1)},
         "gpu_launches": args.steps * len(probs),
         "clocks": clk.summary(),
         "sweep": sweep_detail,
@@ -431,7 +436,11 @@ def run_sweep_backend(args, dist: Dist) -> dict:
             blk = GemmEpilogueBlock(K, N, act)
             init_sweep_block(blk, torch.Generator().manual_seed(len(calls)))
             blk = blk.to(dev, torch.bfloat16).eval()
-            f = blk if be is None else torch.compile(blk, backend=be)
+            # static shapes: the blocks share one class, and dynamo's automatic
+            # dynamic shapes would hand every block after the first shape change
+            # to the backend with symbolic sizes, which both backends' fusion
+            # passes leave to ATen
+            f = blk if be is None else torch.compile(blk, backend=be, dynamic=False)
             calls.append((f, x, r))
             flops += 2.0 * M * N * K
     with torch.no_grad():

@@ -39,13 +39,15 @@ def _dump(gm: fx.GraphModule) -> None:
                 print(f"#   program: {n.meta['b200_program']}")
 
 
-# Graphs this process has compiled through the backend (a diagnostic count:
-# callers check that their calls really went through it).
+# Graphs this process has compiled through the backend, and the fused GEMM
+# nodes in them (diagnostic counts: callers check that their calls really
+# went through the backend and its GEMM kernels).
 GRAPHS_COMPILED = 0
+GEMMS_FUSED = 0
 
 
 def _passes(gm: fx.GraphModule) -> fx.GraphModule:
-    global GRAPHS_COMPILED
+    global GRAPHS_COMPILED, GEMMS_FUSED
     GRAPHS_COMPILED += 1
     if config.EXTENSIONS and config.ENABLE_PATCHIFY:
         gm = fuse_patchify(gm)  # patch-embedding convolutions -> im2col + addmm (extension)
@@ -63,6 +65,8 @@ def _passes(gm: fx.GraphModule) -> fx.GraphModule:
         gm = fuse_epilogue(gm)  # pointwise groups that consume a matmul
     if config.ENABLE_POINTWISE:
         gm = fuse_pointwise(gm)  # the remaining pointwise groups
+    GEMMS_FUSED += sum(1 for n in gm.graph.nodes
+                       if n.op == "call_function" and n.target == torch.ops.b200.gemm_epilogue.default)
     if config.DUMP:
         _dump(gm)
     return gm
