@@ -106,7 +106,6 @@ struct Params {
   const void* bias_ptr;
   int64_t bias_sn;
   int32_t bias_dt;
-  int32_t bias_vec;  // 1: unit stride, 16-byte aligned -- whole 32-column runs load as vectors
   const void* row_ptr;
   int64_t row_sm;
   unsigned long long* trace;                       // diagnostic timeline, null = off
@@ -549,10 +548,12 @@ __device__ __forceinline__ void apply_act8(float (&v)[8]) {
 // ------------------------------------------- fast path, latency-hiding loop
 // Operand staging modes, chosen on the host per operand:
 //   XM_BCAST   row-broadcast f32/bf16/f16 vector (stride_m == 0, e.g. a
-//              bias): every lane loads the sub-chunk's 32 values with
-//              warp-uniform 16-byte loads (L1 hits after the first tile; a
-//              shuffle per value instead costs more than the whole rest of
-//              a bias-only epilogue);
+//              bias): each lane loads one column's value a sub-chunk ahead
+//              and the warp exchanges them through a 128-byte shared slot
+//              (a shuffle per value costs more than the whole rest of a
+//              bias-only epilogue; warp-uniform vector loads at the point of
+//              use, an earlier design, missed L1 and waited on L2 for
+//              600-1400 cycles a sub-chunk);
 //   XM_ROW16   full 16-bit matrix with unit column stride (a residual, or the
 //              `up` operand of SwiGLU): each lane loads its own row's 32
 //              values (64 bytes) into registers;
@@ -579,6 +580,7 @@ enum { ROW_NONE = 0, ROW_SCALE = 1, ROW_RES = 2, ROW_SCALE_PK = 3, ROW_RES_PK = 
 
 struct FastOps {
   uint4 row_r[4];  // the full-matrix operand's 32 values of this lane's row
+  float bias;      // the bias of column n + lane (0 beyond N)
 };
 
 // 32 lanes x 32 bit, 32 consecutive columns.
@@ -607,65 +609,16 @@ __device__ __forceinline__ void tmem_wait_ld_regs(uint32_t (&r)[32]) {
                : "memory");
 }
 
-// Adds the row-broadcast bias of columns n..n+31 to v (every lane the same
-// 32 values).  A run inside [0, N) of a unit-stride, 16-byte-aligned vector
-// loads as 4 (16-bit) or 8 (f32) 16-byte vectors whose address is the same
-// for every lane, one L1 request each; edge runs and strided vectors load
-// value by value.  Each add is rounded on its own (__fadd_rn), as the
-// decomposed graph's bias add is.  (v stays in registers: no call takes it
-// by reference.)
+// The bias of one column as fp32 (0 at and beyond N), any stride and
+// 16/32-bit dtype.  The compiled epilogue loads one column per lane a
+// sub-chunk ahead and adds it rounded on its own (__fadd_rn), as the
+// decomposed graph's bias add is.
 __device__ __forceinline__ float bias_at(const Params& p, int col) {
   if (col >= p.N) return 0.0f;
   const int64_t off = static_cast<int64_t>(col) * p.bias_sn;
   if (p.bias_dt == B200K_F32) return __ldg(reinterpret_cast<const float*>(p.bias_ptr) + off);
   const unsigned short u = __ldg(reinterpret_cast<const unsigned short*>(p.bias_ptr) + off);
   return p.bias_dt == B200K_BF16 ? __uint_as_float(static_cast<uint32_t>(u) << 16) : __half2float(__ushort_as_half(u));
-}
-
-__device__ __forceinline__ void add_bias32(const Params& p, int n, float (&v)[32]) {
-  if (!p.bias_vec || n + 32 > p.N) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __fadd_rn(v[j], bias_at(p, n + j));
-    return;
-  }
-  if (p.bias_dt == B200K_F32) {
-    const float4* q = reinterpret_cast<const float4*>(p.bias_ptr) + (n >> 2);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 b4 = __ldg(q + i);
-      const float b[4] = {b4.x, b4.y, b4.z, b4.w};
-      op2_rn<2, false>(&v[4 * i], b);
-    }
-    return;
-  }
-  const uint4* q = reinterpret_cast<const uint4*>(p.bias_ptr) + (n >> 3);
-  uint4 w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) w[i] = __ldg(q + i);
-  float b[32];
-  if (p.bias_dt == B200K_BF16) {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        b[8 * i + 2 * j] = __uint_as_float(u[j] << 16);
-        b[8 * i + 2 * j + 1] = __uint_as_float(u[j] & 0xffff0000u);
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const uint32_t u[4] = {w[i].x, w[i].y, w[i].z, w[i].w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
-        b[8 * i + 2 * j] = f.x;
-        b[8 * i + 2 * j + 1] = f.y;
-      }
-    }
-  }
-  op2_rn<16, false>(v, b);
 }
 
 // Eight 16-bit values of one row from column n, zero at and beyond column N.
@@ -713,9 +666,15 @@ __device__ __forceinline__ void prefetch_row16_l2(const Params& p, int m, int n)
   prefetch_l2(row + bytes - 1);  // the line of the last byte when the row is not 128-byte aligned
 }
 
+// Issues the loads of the next sub-chunk's operands: this lane's row of the
+// full-matrix operand and the bias of column n + lane.  Their latency (an
+// L2 round trip: the 28 KB of L1 beside 227 KB of shared memory does not
+// keep a bias) then overlaps the current sub-chunk instead of stalling the
+// next.
 template <int ROW>
-__device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, FastOps& f) {
+__device__ __forceinline__ void fast_prefetch(const Params& p, int m, int n, int lane, FastOps& f) {
   if constexpr (ROW != ROW_NONE) load_row16(p.row_ptr, p.row_sm, m, n, p.M, p.N, f.row_r);
+  if (p.f_bias >= 0) f.bias = bias_at(p, n + lane);
 }
 
 __device__ __forceinline__ uint32_t pk_op(uint32_t a, uint32_t b, bool bf16, bool mul) {
@@ -759,7 +718,8 @@ __device__ __forceinline__ void unpack16x8(uint4 u, int dt, float (&x)[8]) {
 // memory by the caller, one sub-chunk ahead of their use).
 template <int BN, int OUT_BYTES, int ACT, int ROW>
 __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMap* tmO, const uint32_t (&raw)[32],
-                                               int row0, int n, int s, int lane, uint8_t* sb, const FastOps& use) {
+                                               int row0, int n, int s, int lane, uint8_t* sb, float* bslot,
+                                               const FastOps& use) {
   constexpr int kEC = 128 / OUT_BYTES;
   constexpr int NSUB = Epi<BN>::CW / 32;
   constexpr int SUB_PER_STG = kEC / 32;
@@ -770,7 +730,19 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
 #pragma unroll
   for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
   const int sub = s % SUB_PER_STG;
-  if (p.f_bias >= 0) add_bias32(p, n, v);
+  if (p.f_bias >= 0) {
+    // Each lane holds the bias of one column (loaded a sub-chunk ahead); the
+    // warp's 128-byte slot hands every lane all 32 (broadcast reads).
+    __syncwarp();  // every lane has read the previous sub-chunk's values
+    bslot[lane] = use.bias;
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 b4 = reinterpret_cast<const float4*>(bslot)[i];
+      const float b[4] = {b4.x, b4.y, b4.z, b4.w};
+      op2_rn<2, false>(&v[4 * i], b);
+    }
+  }
 #pragma unroll
   for (int g = 0; g < 4; ++g) apply_act8<ACT>(*reinterpret_cast<float(*)[8]>(&v[8 * g]));
   const bool out_bf16 = p.out_dt == B200K_BF16;
@@ -857,6 +829,7 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
 template <int BN, int OUT_BYTES, int ACT, int ROW, bool PAIR = false, bool WIDE = false>
 __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
                                                    uint64_t* tfull, uint64_t* tempty, uint64_t* tsoon, uint8_t* sb,
+                                                   float* bslot,
                                                    int quarter, int cg, int lane, const Ctl& ctl,
                                                    uint32_t rank = 0) {
   static_assert(PAIR || !WIDE, "wide tiles run on CTA pairs");
@@ -872,7 +845,7 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
   if (t0 < p.num_tiles) {
     int tm, tn;
     tile_coords(t0, p, tm, tn);
-    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + cg * CW, cur);
+    fast_prefetch<ROW>(p, tm * TM + rank_rows + quarter * 32 + lane, tn * TN + cg * CW, lane, cur);
   }
   int acc = 0;
   uint32_t aph = 0;
@@ -923,9 +896,9 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
       for (int s = 0; s < NSUB; ++s) {
         const int n = n0 + s * 32;
         if (stamper && ti == 0 && h == 0 && s < 4) stamp(p, 248 + 2 * s);
-        if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, nxt);
-        else if (h + 1 < H) fast_prefetch<ROW>(p, m, n0 + BN, nxt);
-        else if (more) fast_prefetch<ROW>(p, m2, n2, nxt);
+        if (s + 1 < NSUB) fast_prefetch<ROW>(p, m, n + 32, lane, nxt);
+        else if (h + 1 < H) fast_prefetch<ROW>(p, m, n0 + BN, lane, nxt);
+        else if (more) fast_prefetch<ROW>(p, m2, n2, lane, nxt);
         if (n < p.N) {  // warp-uniform
           uint32_t now[32];
           if constexpr (kAhead) {
@@ -937,10 +910,10 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
             tmem_ld32(t_row + s * 32, now);
             tmem_wait_ld_regs(now);
           }
-          fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, now, row0, n, s, lane, sb, cur);
+          fast_sub_chunk<BN, OUT_BYTES, ACT, ROW>(p, tmO, now, row0, n, s, lane, sb, bslot, cur);
         }
         if (stamper && ti == 0 && h == 0 && s < 4) stamp(p, 249 + 2 * s);
-        if constexpr (ROW != ROW_NONE) cur = nxt;
+        cur = nxt;
       }
       tc_fence_before();
       __syncwarp();
@@ -969,7 +942,8 @@ struct Cfg {
   static constexpr uint32_t kTmemCols = BN == 128 ? 256 : 512;  // two accumulators, power-of-two allocation
   static constexpr int kEC = 128 / OUT_BYTES;  // output columns per 128-byte staging row
   static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<BN>::kWarps * kStgBytes;
-  static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
+  static constexpr uint32_t kBiasOff = kBarOff + 256;  // one 32-float bias slot per epilogue warp
+  static constexpr uint32_t kSmem = 1024 + kBiasOff + Epi<BN>::kWarps * 128;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
   static_assert(2 * BN <= kTmemCols, "two accumulators fit the allocation");
@@ -1132,6 +1106,7 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
     // ------------------------------------------------------------ epilogue (compiled form)
     const int ew = warp - 4;
     epilogue_fast_loop<BN, OUT_BYTES, ACT, ROW>(p, &tmO, tmem_base, tfull, tempty, tsoon, sStg + ew * kStgBytes,
+                                                reinterpret_cast<float*>(sbase + C::kBiasOff) + 32 * ew,
                                                 warp & 3, ew >> 2, lane, ctl);
     } else {
     // ------------------------------------------------------------ epilogue (interpreted program)
@@ -1232,7 +1207,8 @@ struct PairCfg {
   static constexpr uint32_t kBBytes = kHalves * kBHalfBytes;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kBarOff = STAGES * (kABytes + kBBytes) + Epi<kPairMmaN>::kWarps * kStgBytes;
-  static constexpr uint32_t kSmem = 1024 + kBarOff + 256;
+  static constexpr uint32_t kBiasOff = kBarOff + 256;  // one 32-float bias slot per epilogue warp
+  static constexpr uint32_t kSmem = 1024 + kBiasOff + Epi<kPairMmaN>::kWarps * 128;
   static_assert(kSmem <= 232448, "shared memory budget");
   static_assert(kSmem > 232448 / 2, "one CTA per SM keeps the TMEM allocation uncontended");
 };
@@ -1406,7 +1382,10 @@ __global__ void __launch_bounds__(Epi<kPairMmaN>::kThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int ew = warp - 4;
     epilogue_fast_loop<kPairMmaN, OUT_BYTES, ACT, ROW, true, WIDE>(p, &tmO, tmem_base, tfull, tempty, tsoon,
-                                                                   sStg + ew * kStgBytes, warp & 3, ew >> 2, lane,
+                                                                   sStg + ew * kStgBytes,
+                                                                   reinterpret_cast<float*>(sbase + C::kBiasOff) +
+                                                                       32 * ew,
+                                                                   warp & 3, ew >> 2, lane,
                                                                    ctl, rank);
   }
 

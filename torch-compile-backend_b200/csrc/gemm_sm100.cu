@@ -409,7 +409,6 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     p.bias_ptr = e.ptr;
     p.bias_sn = e.stride_n;
     p.bias_dt = e.dtype;
-    p.bias_vec = e.stride_n == 1 && aligned16(e.ptr) ? 1 : 0;
   }
   p.xm_scale = mode_of(a->form.scale, true);
   p.xm_res = mode_of(a->form.residual, true);
