@@ -791,7 +791,7 @@ def _host_threads() -> int:
     return n
 
 
-def run_reference_cpu(steps: int, warmup: int, rows: int) -> dict:
+def run_reference_cpu(steps: int, warmup: int, rows: int, models: bool = True) -> dict:
     """The reference's own CPU path for the sweep on the host cores.
 
     Each block runs through ``torch.compile(block, backend=custom_backend)``
@@ -802,7 +802,9 @@ def run_reference_cpu(steps: int, warmup: int, rows: int) -> dict:
     sweep's own ATen graph, with every host thread.  A step runs the first
     `rows` rows of each of the twelve sweep GEMMs (the 512^3 points whole);
     the value is the sampled FLOPs / median step time.  Without the reference
-    install the same blocks run eagerly (kind "port")."""
+    install the same blocks run eagerly (kind "port").  With `models`, the
+    MLP, ViT-B/16 and Llama-style forwards on the host cores are added
+    (run_models_cpu)."""
     from bench_models import GemmEpilogueBlock, init_sweep_block
 
     threads = _host_threads()
@@ -839,10 +841,84 @@ def run_reference_cpu(steps: int, warmup: int, rows: int) -> dict:
             times.append(time.perf_counter() - t0)
     flops = sum(w[3] for w in work)
     med = statistics.median(times)
-    return {"value": round(flops / med / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind,
-            "sample": f"first {rows} rows of each of the 12 sweep GEMMs (512^3 whole), bf16, "
-                      f"median of {len(times)} steps of {med * 1e3:.0f} ms; reference backend on CPU = "
-                      "eager ATen graph", "ms_per_step": round(med * 1e3, 2)}
+    res = {"value": round(flops / med / 1e12, 4), "unit": "TFLOP/s", "cores": threads, "kind": kind,
+           "sample": f"first {rows} rows of each of the 12 sweep GEMMs (512^3 whole), bf16, "
+                     f"median of {len(times)} steps of {med * 1e3:.0f} ms; reference backend on CPU = "
+                     "eager ATen graph", "ms_per_step": round(med * 1e3, 2)}
+    if models:
+        try:
+            res["models"] = run_models_cpu()
+        except Exception as e:  # noqa: BLE001 -- recorded in the line
+            res["models"] = {"unavailable": f"{type(e).__name__}: {e}"[:300]}
+    return res
+
+
+def _median_s(fn, reps: int, warm: int) -> float:
+    for _ in range(warm):
+        fn()
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts)
+
+
+def _fill_cpu(model: torch.nn.Module) -> torch.nn.Module:
+    """Materialises a meta-device model on the CPU in bf16: matrices and
+    embeddings tile one seeded N(0, 0.02) block, vectors are ones (norm
+    weights) or the same block (biases)."""
+    model = model.to_empty(device="cpu").to(torch.bfloat16)
+    block = (0.02 * torch.randn(1 << 20, generator=torch.Generator().manual_seed(0))).to(torch.bfloat16)
+    with torch.no_grad():
+        for name, p in model.named_parameters():
+            if p.dim() == 1 and name.endswith("weight"):
+                p.fill_(1.0)
+                continue
+            flat = p.view(-1)
+            for i in range(0, flat.numel(), block.numel()):
+                n = min(block.numel(), flat.numel() - i)
+                flat[i:i + n].copy_(block[:n])
+    return model
+
+
+def run_models_cpu() -> dict:
+    """The benchmark's models forward on the host cores: the eager graph,
+    i.e. the ATen ops the reference backend leaves unfused on CPU (its passes
+    need CUDA values), run without the compile step to keep the leg short.
+    The MLP runs at its full configuration (x[64,1024] fp32, median of 20);
+    ViT-B/16 on 2 of the 64 images and the Llama-style prefill on one
+    256-token sequence (bf16, median of 3): tokens/s of those samples."""
+    import bench_models as bm
+
+    out = {}
+    with torch.no_grad():
+        torch.manual_seed(0)
+        mlp = bm.MLP().eval()
+        x = torch.randn(64, 1024, generator=torch.Generator().manual_seed(0))
+        t = _median_s(lambda: mlp(x), 20, 3)
+        out["mlp"] = {"ms": round(t * 1e3, 3), "rows_per_s": round(64 / t, 1),
+                      "tflops": round(bm.mlp_flops() / t / 1e12, 4), "sample": "full config, fp32"}
+        # The big models are built on the meta device and filled by tiling one
+        # seeded N(0, 0.02) block: drawing 1.5e9 values one by one takes minutes
+        # on the host, and the timing does not depend on the values.
+        with torch.device("meta"):
+            vit, llama = bm.ViT(), bm.Llama()
+        vit, llama = _fill_cpu(vit), _fill_cpu(llama)
+        llama.reset_rope()
+        vit.eval()
+        img = torch.randn(2, 3, 224, 224, generator=torch.Generator().manual_seed(0)).to(torch.bfloat16)
+        t = _median_s(lambda: vit(img), 3, 1)
+        out["vit"] = {"ms": round(t * 1e3, 2), "tokens_per_s": round(2 * 197 / t, 1),
+                      "tflops": round(2 * bm.vit_flops_per_image() / t / 1e12, 4), "sample": "batch 2 of 64, bf16"}
+        del vit
+        llama.eval()
+        ids = torch.randint(0, 128256, (1, 256), generator=torch.Generator().manual_seed(0))
+        t = _median_s(lambda: llama(ids), 3, 1)
+        out["llama"] = {"ms": round(t * 1e3, 1), "tokens_per_s": round(256 / t, 1),
+                        "tflops": round(bm.llama_flops_per_token(seq=256) * 256 / t / 1e12, 4),
+                        "sample": "1 sequence x 256 tokens of 8 x 2048, bf16"}
+    return out
 
 
 def _cpu_baseline_subprocess(rows: int) -> dict | None:
@@ -961,6 +1037,8 @@ def main() -> None:
                     help="gemm workload: out = x w^T with no epilogue, against torch.mm in the eager leg")
     ap.add_argument("--cpu-rows", type=int, default=1024, help="rows of each sweep GEMM the CPU leg runs")
     ap.add_argument("--model-steps", type=int, default=10, help="timed steps of each model extra")
+    ap.add_argument("--no-cpu-models", dest="cpu_models", action="store_false",
+                    help="reference arm: skip the MLP / ViT / Llama forward on the host cores")
     ap.add_argument("--no-extras", action="store_true",
                     help="sweep only: skip the ViT/Llama/chain extras and the CPU baseline")
     ap.add_argument("--no-reference-models", dest="reference_models", action="store_false",
@@ -973,14 +1051,15 @@ def main() -> None:
     if args.impl == "reference":
         if dist_env_rank != 0:
             return
-        base = run_reference_cpu(args.steps, args.warmup, args.cpu_rows)
+        base = run_reference_cpu(args.steps, args.warmup, args.cpu_rows, args.cpu_models)
         line = {"impl": "reference", "metric": "fused GEMM+epilogue TFLOP/s", "value": base["value"],
                 "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
                 "ms_per_step": base["ms_per_step"], "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,0.02) X/W/R, N(0,0.01) b)",
                 "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS,
                            "epilogue": "act(X W^T + b) + R, bf16 in/out", "sample_rows": args.cpu_rows},
-                "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "models")
+                                 if k in base},
                 "e2e": {"value": base["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                         "d2h_bytes_per_step": 0}}
         print(json.dumps(line))

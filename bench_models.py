@@ -39,6 +39,26 @@ def init_sweep_block(block: GemmEpilogueBlock, gen: torch.Generator) -> None:
         block.lin.bias.normal_(0.0, 0.01, generator=gen)
 
 
+# --------------------------------------------------------------------- MLP
+class MLP(nn.Module):
+    """The benchmark's MLP configuration: x[64,1024] fp32 ->
+    Linear(1024->4096) -> GELU(tanh) -> Linear(4096->1024) -> + x, with
+    nn.Linear's default init.  The reference's bench/mlp.py:6-19 block has
+    the same GEMM shapes with an erf GELU and an x + tanh(y) * scale tail."""
+
+    def __init__(self, dim=1024, hidden=4096):
+        super().__init__()
+        self.fc1 = nn.Linear(dim, hidden)
+        self.fc2 = nn.Linear(hidden, dim)
+
+    def forward(self, x):
+        return self.fc2(F.gelu(self.fc1(x), approximate="tanh")) + x
+
+
+def mlp_flops(rows=64, dim=1024, hidden=4096) -> float:
+    return 2.0 * rows * dim * hidden * 2
+
+
 # --------------------------------------------------------------------- ViT
 class ViTBlock(nn.Module):
     def __init__(self, dim: int, heads: int, mlp: int):
@@ -147,12 +167,21 @@ class Llama(nn.Module):
         self.layers = nn.ModuleList(LlamaLayer(dim, heads, kv_heads, ffn, eps) for _ in range(layers))
         self.norm = RMSNorm(dim, eps)
         self.lm_head = nn.Linear(dim, vocab, bias=False)
-        hd = dim // heads
-        inv = 1.0 / (theta ** (torch.arange(0, hd, 2, dtype=torch.float32) / hd))
-        f = torch.outer(torch.arange(max_seq, dtype=torch.float32), inv)
+        self.hd, self.theta, self.max_seq = dim // heads, theta, max_seq
+        self.register_buffer("cos", torch.empty(max_seq, self.hd, dtype=torch.float32), persistent=False)
+        self.register_buffer("sin", torch.empty(max_seq, self.hd, dtype=torch.float32), persistent=False)
+        self.reset_rope()
+
+    def reset_rope(self) -> None:
+        """(Re)computes the rotary tables (also after materialising a model
+        built on the meta device)."""
+        hd, dev = self.hd, self.cos.device
+        inv = 1.0 / (self.theta ** (torch.arange(0, hd, 2, dtype=torch.float32, device=dev) / hd))
+        f = torch.outer(torch.arange(self.max_seq, dtype=torch.float32, device=dev), inv)
         emb = torch.cat([f, f], dim=-1)
-        self.register_buffer("cos", emb.cos(), persistent=False)
-        self.register_buffer("sin", emb.sin(), persistent=False)
+        with torch.no_grad():
+            self.cos.copy_(emb.cos())
+            self.sin.copy_(emb.sin())
 
     def forward(self, ids):
         S = ids.shape[1]

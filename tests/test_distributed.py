@@ -51,7 +51,7 @@ def test_reference_arm_under_torchrun_prints_once():
     cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node", "2",
            "--master-addr", "127.0.0.1", "--master-port", str(_free_port()),
            os.path.join(ROOT, "bench.py"), "--impl", "reference", "--gpus", "2", "--steps", "1", "--warmup", "0",
-           "--cpu-rows", "4"]
+           "--cpu-rows", "4", "--no-cpu-models"]
     r = subprocess.run(cmd, capture_output=True, text=True, timeout=600, cwd=ROOT)
     assert r.returncode == 0, r.stderr[-2000:]
     lines = [line for line in r.stdout.splitlines() if line.startswith("{")]
@@ -61,3 +61,15 @@ def test_reference_arm_under_torchrun_prints_once():
     assert d["cpu_baseline"]["kind"] in ("reference", "port") and d["e2e"]["h2d_bytes_per_step"] == 0
     # torchrun pins OMP_NUM_THREADS=1; the CPU leg uses every host thread anyway
     assert d["cpu_baseline"]["cores"] == len(os.sched_getaffinity(0))
+
+
+def test_cpu_model_baselines():
+    """The reference arm's model leg: the MLP config and the ViT / Llama
+    samples run forward on the host cores and report tokens/s."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    d = bench.run_models_cpu()
+    assert d["mlp"]["rows_per_s"] > 0 and "full config" in d["mlp"]["sample"]
+    assert d["vit"]["tokens_per_s"] > 0 and d["llama"]["tokens_per_s"] > 0
+    assert all(0 < d[k]["tflops"] < 100 for k in ("mlp", "vit", "llama"))
