@@ -207,9 +207,12 @@ typedef struct {
 /*
  * out[m,n] = program(acc[m,n], extras[..][m,n]) with acc = sum_k a[m,k]*b[k,n]
  * accumulated in fp32 on the tcgen05 tensor cores.  a is [M,K] with unit K
- * stride; b is the reference's mat2 [K,N] (usually t(W) with unit K stride,
- * "K-major"; unit N stride, "N-major", is also accepted).  a/b dtype: f16 or
- * bf16.  out: f16, bf16 or f32 with unit N stride.
+ * stride, or (16-bit, interpreted epilogues) unit M stride -- the transposed
+ * gradient of a backward graph's weight-gradient mm; b is the reference's
+ * mat2 [K,N] (usually t(W) with unit K stride, "K-major"; unit N stride,
+ * "N-major", is also accepted).  a/b dtype: f16 or bf16, or f32 on the TF32
+ * tensor cores (K-major a and b).  out: f16, bf16 or f32 with unit N
+ * stride.
  * Replaces fusion_epilogue.py:72-151 (kernel), :164-177 (launch) and the
  * AUTOTUNE_CONFIGS table (:31-38) with a fixed B200 tile table.
  */

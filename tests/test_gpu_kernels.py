@@ -316,13 +316,60 @@ def test_gemm_repeated_calls_reuse_nothing_stale():
 
 
 def test_gemm_rejects_bad_layout():
-    """A with a non-unit K stride is refused with an error code, not computed wrongly."""
-    x = torch.randn(64, 64, device=DEV).to(torch.bfloat16).t()  # strides (1, 64)
+    """A with neither a unit K nor a unit M stride is refused with an error
+    code, not computed wrongly; so is an fp32 M-major A (TF32 runs K-major
+    operands only)."""
+    x = torch.randn(64, 128, device=DEV).to(torch.bfloat16)[:, ::2]  # strides (128, 2)
     w = torch.randn(56, 64, device=DEV).to(torch.bfloat16)
     out = torch.empty(64, 56, device=DEV, dtype=torch.bfloat16)
     with pytest.raises(cabi.CError) as e:
         cabi.gemm_epilogue(x, w.t(), [], [], [], out)
     assert e.value.code == 4
+    xf = torch.randn(64, 64, device=DEV).t()  # fp32, strides (1, 64)
+    outf = torch.empty(64, 56, device=DEV)
+    with pytest.raises(cabi.CError) as e:
+        cabi.gemm_epilogue(xf, torch.randn(56, 64, device=DEV).t(), [], [], [], outf)
+    assert e.value.code == 4
+
+
+@pytest.mark.parametrize("M,N,K", [(37, 72, 24), (128, 256, 64), (130, 260, 72), (300, 100, 136),
+                                   (1000, 768, 264), (999, 768, 257), (2048, 1024, 4096)])
+@pytest.mark.parametrize("b_layout", ["k_major", "n_major"])
+@pytest.mark.parametrize("config", [0, 1, 3])
+@pytest.mark.parametrize("ab", ["bfloat16", "float16"])
+def test_gemm_m_major_a(M, N, K, b_layout, config, ab):
+    """A stored M-major (unit M stride: the transposed gradient that a
+    backward graph's weight-gradient mm reads), with K-major and N-major B,
+    ragged shapes, gelu-tanh + bias + residual (interpreted), against the
+    oracle; a forced CTA-pair config runs 128-row tiles."""
+    dt = _tdt(ab)
+    g = torch.Generator(device=DEV).manual_seed(M + 3 * N + K)
+    m_pad = (M + 7) // 8 * 8  # the K stride (elements) keeps 16-byte rows
+    x = torch.randn(K, m_pad, device=DEV, generator=g).to(dt)[:, :M].t()  # [M, K], strides (1, m_pad)
+    assert x.stride() == (1, m_pad)
+    w = torch.randn(N, K, device=DEV, generator=g).to(dt)
+    # B [K, N] as t(W) (K-major) or row-major (N-major), rows padded to 16 bytes
+    k_pad, n_pad = (K + 7) // 8 * 8, (N + 7) // 8 * 8
+    if b_layout == "k_major":
+        bmat = torch.zeros(N, k_pad, device=DEV, dtype=dt)[:, :K].copy_(w).t()
+    else:
+        bmat = torch.zeros(K, n_pad, device=DEV, dtype=dt)[:, :N].copy_(w.t())
+    b = torch.randn(N, device=DEV, generator=g).to(dt)
+    r = torch.randn(M, N, device=DEV, generator=g).to(dt)
+    code, imm, spec, form = epilogue_program("gelu_tanh", residual=True)
+    out = torch.empty(M, N, device=DEV, dtype=dt)
+    cabi.gemm_epilogue(x, bmat, [b, r], code, imm, out, tile_config=config, form=form)
+    torch.cuda.synchronize()
+    want = oracle.gemm_epilogue(x.float().cpu().numpy(), w.float().cpu().numpy().T, spec,
+                                [b.float().cpu().numpy(), r.float().cpu().numpy()], ab, bias=b.float().cpu().numpy())
+    _assert_close(out, want, *_gemm_tol(want))
+    if (K * x.element_size()) % 16:
+        return  # a K-major copy of A would not have 16-byte rows
+    # the same product from a K-major copy of A is bit-identical (same tiles, same MMA order)
+    out2 = torch.empty_like(out)
+    cabi.gemm_epilogue(x.contiguous(), bmat, [b, r], code, imm, out2, tile_config=config, form=None)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out2)
 
 
 # ------------------------------------------------------------- pointwise

@@ -125,6 +125,66 @@ def test_training_step_grads_match_eager():
     assert _rel(model.fc2.bias.grad, ref.fc2.bias.grad) < 3e-2
 
 
+def _training_grads(model, inputs, n_graphs=2):
+    """One forward + backward of `model` compiled with the backend (forward
+    and backward graphs through the passes) and of an fp32 copy run eagerly;
+    returns (graphs, [(name, grad, fp32 grad)], (input grad, fp32 input grad))."""
+    import copy
+
+    ref = copy.deepcopy(model).float()
+    x = inputs[0].detach().clone().requires_grad_(True)
+    xr = inputs[0].detach().float().clone().requires_grad_(True)
+    torch._dynamo.reset()
+    be, graphs = capturing_backend()
+    out = torch.compile(model, backend=be)(x, *inputs[1:])
+    want = ref(xr, *[t.float() for t in inputs[1:]])
+    wgt = torch.randn(out.shape, device=DEV, generator=torch.Generator(device=DEV).manual_seed(7))
+    (out.float() * wgt).sum().backward()
+    (want * wgt).sum().backward()
+    runtime.check_status()
+    assert len(graphs) == n_graphs  # the backward graph went through the compiler too
+    assert _rel(out, want) < 2e-2
+    pairs = [(n, p.grad, dict(ref.named_parameters())[n].grad) for n, p in model.named_parameters()]
+    return graphs, pairs, (x.grad, xr.grad)
+
+
+def test_vit_block_training_step_matches_fp32_eager():
+    """A ViT-B/16-style block (bf16, training): every parameter and input
+    gradient against the same block in fp32, eager; the backward graph's
+    gradient accumulations run as fused kernels."""
+    torch.manual_seed(0)
+    model = bm.ViTBlock(256, 4, 1024).to(DEV, torch.bfloat16)
+    x = torch.randn(4, 65, 256, device=DEV, dtype=torch.bfloat16)
+    graphs, pairs, (gx, gx_ref) = _training_grads(model, (x,))
+    assert len(pairs) == 12
+    for name, got, want in pairs:
+        assert _rel(got, want) < 3e-2, name
+    assert _rel(gx, gx_ref) < 3e-2
+    bw = [str(t) for t in b200_targets(graphs[1:])]
+    assert "b200.pointwise.default" in bw
+
+
+def test_llama_layer_training_step_matches_fp32_eager():
+    """A Llama-style decoder layer (bf16, training, GQA, RoPE): every
+    parameter and input gradient against fp32 eager; the backward graph's
+    input-gradient GEMMs that feed gradient sums run with that sum as their
+    epilogue."""
+    torch.manual_seed(0)
+    model = bm.LlamaLayer(256, 4, 2, 512, 1e-5)
+    bm.init_normal_(model, 0.02, torch.Generator().manual_seed(0))
+    model = model.to(DEV, torch.bfloat16)
+    tables = bm.Llama(vocab=16, dim=256, layers=0, heads=4, kv_heads=2, ffn=512, max_seq=128)
+    cos, sin = (t.to(DEV, torch.bfloat16) for t in (tables.cos, tables.sin))
+    x = torch.randn(2, 128, 256, device=DEV, dtype=torch.bfloat16)
+    graphs, pairs, (gx, gx_ref) = _training_grads(model, (x, cos, sin))
+    assert len(pairs) == 9
+    for name, got, want in pairs:
+        assert _rel(got, want) < 3e-2, name
+    assert _rel(gx, gx_ref) < 3e-2
+    bw = [str(t) for t in b200_targets(graphs[1:])]
+    assert bw.count("b200.gemm_epilogue.default") >= 2
+
+
 def test_hand_written_api():
     from hand_written.gemm_kernel import gemm
     from hand_written.gemm_swizzled_kernel import gemm as gemm_sw

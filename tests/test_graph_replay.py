@@ -231,3 +231,13 @@ def test_split_replay_matches_op_by_op_and_outputs_survive_later_calls(monkeypat
     torch._dynamo.reset()
     for o, w in zip(outs, want):
         assert torch.equal(o, w)
+
+
+def test_boxed_marker_survives_wrapping():
+    """AOTAutograd reaches a backward graph's callable through a
+    functools.wraps wrapper (torch._dynamo.disable); the list-argument marker
+    has to survive it, or the backward call passes unpacked arguments."""
+    from compiler.backend import StatusChecked
+
+    for obj in (StatusChecked(lambda a: a, 0), graph_replay.GraphReplay(lambda a: a)):
+        assert getattr(torch._dynamo.disable(obj), "_boxed_call", False)

@@ -552,3 +552,24 @@ def test_fp32_epilogue_fusion_follows_allow_tf32():
     finally:
         torch.backends.cuda.matmul.allow_tf32 = old
     assert counts[True] >= 1 and counts[False] == 0
+
+
+def test_transposed_a_matmul_with_pointwise_tail_is_fused():
+    """mm(t(g), x) -- the weight-gradient product of a backward graph -- with
+    a pointwise consumer reaches the library (A read M-major), as the
+    reference's anchor takes any 2-d mm with a pointwise tail
+    (compiler/optimization/fusion_epilogue.py:45-69); an fp32 one without
+    TF32 stays ATen."""
+
+    class WGrad(nn.Module):
+        def forward(self, g, x, c):
+            return (g.t() @ x) * 0.5 + c
+
+    g, x = torch.randn(96, 32).to(torch.bfloat16), torch.randn(96, 48).to(torch.bfloat16)
+    c = torch.randn(32, 48).to(torch.bfloat16)
+    nodes = _epi_nodes(WGrad(), (g, x, c))
+    assert len(nodes) == 1
+    a = nodes[0].args[0].meta["val"]
+    assert a.shape == (32, 96) and a.stride() == (1, 32)
+    (gm,) = fused_graphs(WGrad(), (g.float(), x.float(), c.float()))
+    assert torch.ops.b200.gemm_epilogue.default not in _targets(gm)

@@ -81,11 +81,14 @@ class StatusChecked:
     graph with no error; with it the error surfaces at the next compiled
     call (or at ``runtime.check_status()``, which synchronises)."""
 
-    _boxed_call = True
-
     def __init__(self, fn, device: int):
         self.fn = fn
         self.device = device
+        # AOTAutograd's marker for the list-argument calling convention, on
+        # the instance: the backward graph's callable reaches AOTAutograd
+        # through a functools.wraps wrapper, which copies the instance's
+        # __dict__ but not class attributes.
+        self._boxed_call = True
 
     def __call__(self, args):
         torch.ops.b200.status_check(self.device, False)

@@ -75,9 +75,10 @@ def _is_persistent(t: torch.Tensor) -> bool:
 class GraphReplay:
     """Boxed callable: ``run(args)`` with ``args`` the graph's input list."""
 
-    _boxed_call = True  # AOTAutograd's marker for the list-argument calling convention
-
     def __init__(self, fn, no_clone=()):
+        # AOTAutograd's marker for the list-argument calling convention (an
+        # instance attribute, so that functools.wraps wrappers copy it)
+        self._boxed_call = True
         self.fn = fn  # boxed op-by-op function of the compiled graph
         self.no_clone = frozenset(no_clone)  # output indices returned as the graph's own buffers
         self.calls = 0
@@ -186,9 +187,8 @@ class TailReplay:
     """Boxed callable of a split graph: the body replayed (GraphReplay), then
     the tail op by op on the body's values and the graph's inputs."""
 
-    _boxed_call = True
-
     def __init__(self, body: GraphReplay, tail_gm: fx.GraphModule, n_body_outs: int, plan, tail_args):
+        self._boxed_call = True  # as GraphReplay's
         self.body = body
         self.tail_gm = tail_gm
         self.n_body_outs = n_body_outs  # body outputs that are graph outputs

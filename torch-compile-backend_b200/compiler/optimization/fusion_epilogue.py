@@ -55,7 +55,11 @@ def _kernel_supports(mat1, mat2, out_meta, extras_meta, out_shape) -> bool:
     if min(M, N, K) == 0:
         return False
     eb = a.element_size()
-    if a.stride(1) != 1 or (a.stride(0) * eb) % 16 != 0:
+    a_k_major = a.stride(1) == 1 and (a.stride(0) * eb) % 16 == 0
+    # M-major A (the transposed gradient of a weight-gradient GEMM in a
+    # backward graph): 16-bit only, interpreted epilogue
+    a_m_major = a.stride(0) == 1 and (a.stride(1) * eb) % 16 == 0 and eb == 2
+    if not (a_k_major or a_m_major):
         return False
     k_major = b.stride(0) == 1 and (b.stride(1) * eb) % 16 == 0
     n_major = b.stride(1) == 1 and (b.stride(0) * eb) % 16 == 0 and eb == 2  # TF32 runs K-major B only

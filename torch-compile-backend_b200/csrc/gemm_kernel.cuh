@@ -952,7 +952,12 @@ struct Cfg {
 // TF32: fp32 A and B (K-major B only); a K block is then 32 elements, the
 // same 128 bytes a row as 64 16-bit ones, so the shared-memory layout,
 // descriptors and stage sizes are those of the 16-bit kernel.
-template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW, bool TF32 = false>
+// A_MMAJOR: A is stored M-major (unit M stride, e.g. the transposed gradient
+// of a weight-gradient GEMM), loaded as two 64-row by BK-column boxes whose
+// 128-byte rows run along M, the mirror of N-major B; the instruction
+// descriptor's A-major bit tells the MMA (16-bit operands only).
+template <int BN, int STAGES, bool B_NMAJOR, int OUT_BYTES, bool FAST, int ACT, int ROW, bool TF32 = false,
+          bool A_MMAJOR = false>
 __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
     gemm_epilogue_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                          const __grid_constant__ CUtensorMap tmO, const __grid_constant__ Params p) {
@@ -1027,7 +1032,14 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
           mbar_arrive_expect_tx(&full[s], C::kABytes + C::kBBytes);
           constexpr int kKb = TF32 ? BK / 2 : BK;  // elements of a K block
           static_assert(!(TF32 && B_NMAJOR), "TF32 runs K-major B only");
-          tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kKb, tm * BM);
+          static_assert(!(TF32 && A_MMAJOR), "TF32 runs K-major A only");
+          if (A_MMAJOR) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j)
+              tma_load_2d(sA + s * C::kABytes + j * (64 * BK * 2), &tmA, &full[s], tm * BM + j * 64, kb * BK);
+          } else {
+            tma_load_2d(sA + s * C::kABytes, &tmA, &full[s], kb * kKb, tm * BM);
+          }
           if (B_NMAJOR) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
@@ -1075,7 +1087,8 @@ __global__ void __launch_bounds__(Epi<BN>::kThreads, 1)
           const uint32_t b0 = smem_u32(sB + s * C::kBBytes);
 #pragma unroll
           for (int k = 0; k < BK / UMMA_K; ++k) {
-            const uint64_t ad = sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024);
+            const uint64_t ad = A_MMAJOR ? sw128_desc(a0 + k * (UMMA_K * 128), 64 * BK * 2, 1024)
+                                         : sw128_desc(a0 + k * (UMMA_K * 2), 16, 1024);
             const uint64_t bd = B_NMAJOR ? sw128_desc(b0 + k * (UMMA_K * 128), 64 * BK * 2, 1024)
                                          : sw128_desc(b0 + k * (UMMA_K * 2), 16, 1024);
             if constexpr (TF32) umma_tf32(d_tmem, ad, bd, p.idesc, (kb | k) != 0 ? 1u : 0u);
@@ -1436,11 +1449,11 @@ struct TileConfig {
 constexpr TileConfig kConfigs[] = {{128, 256, 4}, {128, 128, 6}, {128, 192, 4}, {256, 256, 6}, {256, 512, 4}};
 constexpr int kNumConfigs = sizeof(kConfigs) / sizeof(kConfigs[0]);
 
-template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW, bool TF32 = false>
+template <int BN, int STAGES, bool BNM, int OB, bool FAST, int ACT, int ROW, bool TF32 = false, bool AMM = false>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to, const Params& p, int grid,
                cudaStream_t st) {
   using C = Cfg<BN, STAGES, BNM, OB>;
-  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT, ROW, TF32>;
+  auto kern = gemm_epilogue_kernel<BN, STAGES, BNM, OB, FAST, ACT, ROW, TF32, AMM>;
   static bool attr_set = false;  // per instantiation; idempotent
   if (!attr_set) {
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem) != cudaSuccess)

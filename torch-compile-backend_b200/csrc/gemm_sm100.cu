@@ -143,8 +143,16 @@ int check_form_cached(const B200kEpilogueForm& f, const B200kProgram& prog, int 
 }
 
 template <int BN, int STAGES>
-int launch_interp(bool tf32, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& to,
-                  const Params& p, int grid, cudaStream_t st) {
+int launch_interp(bool tf32, bool amm, bool bnm, int ob, const CUtensorMap& ta, const CUtensorMap& tb,
+                  const CUtensorMap& to, const Params& p, int grid, cudaStream_t st) {
+  if (amm) {  // M-major A (16-bit): interpreted epilogues only
+    if (tf32) return B200K_ERR_UNSUPPORTED;
+    if (bnm)
+      return ob == 2 ? launch_one<BN, STAGES, true, 2, false, -1, ROW_NONE, false, true>(ta, tb, to, p, grid, st)
+                     : launch_one<BN, STAGES, true, 4, false, -1, ROW_NONE, false, true>(ta, tb, to, p, grid, st);
+    return ob == 2 ? launch_one<BN, STAGES, false, 2, false, -1, ROW_NONE, false, true>(ta, tb, to, p, grid, st)
+                   : launch_one<BN, STAGES, false, 4, false, -1, ROW_NONE, false, true>(ta, tb, to, p, grid, st);
+  }
   if (tf32) {  // fp32 operands on TF32 tensor cores, K-major B
     if (bnm) return B200K_ERR_UNSUPPORTED;
     return ob == 2 ? launch_one<BN, STAGES, false, 2, false, -1, ROW_NONE, true>(ta, tb, to, p, grid, st)
@@ -300,9 +308,19 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     if (rc != B200K_OK) return rc;
   }
 
-  // A: [M, K], unit K stride, rows 16-byte aligned.
-  if (a->a_stride_k != 1 && a->K > 1) return B200K_ERR_UNSUPPORTED;
-  if (!aligned16(a->a) || (a->a_stride_m * eb) % 16 != 0) return B200K_ERR_ALIGN;
+  // A: [M, K], K-major (unit K stride, rows 16-byte aligned) or M-major
+  // (unit M stride, 16-bit only: the transposed operand of a weight-gradient
+  // GEMM).
+  bool amm;
+  if (a->a_stride_k == 1 || a->K == 1) {
+    amm = false;
+    if (!aligned16(a->a) || (a->a_stride_m * eb) % 16 != 0) return B200K_ERR_ALIGN;
+  } else if (a->a_stride_m == 1 && !tf32) {
+    amm = true;
+    if (!aligned16(a->a) || (a->a_stride_k * eb) % 16 != 0) return B200K_ERR_ALIGN;
+  } else {
+    return B200K_ERR_UNSUPPORTED;
+  }
   // B: K-major (unit K stride) or N-major (unit N stride; 16-bit only).
   bool bnm;
   if (a->b_stride_k == 1) {
@@ -342,7 +360,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const bool row_ok = role_idx < 0 || (ob == 2 && mode_of(role_idx, true) == XM_ROW16 &&
                                        a->extras[role_idx].dtype == a->out_dtype);
   const int bias_mode = mode_of(a->form.bias, false);
-  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) &&
+  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) && !amm &&
                     (bias_mode == XM_NONE || bias_mode == XM_BCAST);
 
   const bool pair_ok = fast && !bnm && ob == 2 && !tf32;  // the CTA-pair kernels' domain
@@ -381,7 +399,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   p.test_flags = a->test_flags;
   // operand format of the instruction descriptor: f16 0 / bf16 1 (kind::f16), tf32 2 (kind::tf32)
   const uint32_t fmt = tf32 ? 2u : (a->ab_dtype == B200K_BF16 ? 1u : 0u);
-  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((bnm ? 1u : 0u) << 16) |
+  p.idesc = (1u << 4) | (fmt << 7) | (fmt << 10) | ((amm ? 1u : 0u) << 15) | ((bnm ? 1u : 0u) << 16) |
             (static_cast<uint32_t>(mma_n >> 3) << 17) | (static_cast<uint32_t>(bm >> 4) << 24);
   p.group_m = pair ? kGroupMPair : kGroupM;
   for (int i = 0; i < a->n_extras; ++i) {
@@ -416,7 +434,11 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
 
   CUtensorMap ta, tb, to;
   std::memset(&to, 0, sizeof(to));
-  if (!make_map(&ta, a->ab_dtype, a->a, a->K, a->M, a->a_stride_m * eb, kb_elems, BM)) return B200K_ERR_LAUNCH;
+  if (amm) {
+    if (!make_map(&ta, a->ab_dtype, a->a, a->M, a->K, a->a_stride_k * eb, 64, BK)) return B200K_ERR_LAUNCH;
+  } else {
+    if (!make_map(&ta, a->ab_dtype, a->a, a->K, a->M, a->a_stride_m * eb, kb_elems, BM)) return B200K_ERR_LAUNCH;
+  }
   if (bnm) {
     if (!make_map(&tb, a->ab_dtype, a->b, a->N, a->K, a->b_stride_k * eb, 64, BK)) return B200K_ERR_LAUNCH;
   } else {
@@ -450,8 +472,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
     if (rc != B200K_ERR_UNSUPPORTED || !tf32) return rc;
     // TF32 forms without a compiled kernel (a row operand, 16-bit output) interpret the program
   }
-  if (cfg == 0 || bn == 192) return launch_interp<256, 4>(tf32, bnm, ob, ta, tb, to, p, grid, st);
-  return launch_interp<128, 6>(tf32, bnm, ob, ta, tb, to, p, grid, st);
+  if (cfg == 0 || bn == 192) return launch_interp<256, 4>(tf32, amm, bnm, ob, ta, tb, to, p, grid, st);
+  return launch_interp<128, 6>(tf32, amm, bnm, ob, ta, tb, to, p, grid, st);
 }
 
 // ---------------------------------------------------------------------------
