@@ -241,3 +241,72 @@ def test_boxed_marker_survives_wrapping():
 
     for obj in (StatusChecked(lambda a: a, 0), graph_replay.GraphReplay(lambda a: a)):
         assert getattr(torch._dynamo.disable(obj), "_boxed_call", False)
+
+
+class _BlocksWithBuffer(_Blocks):
+    """_Blocks with a per-channel scale held as a module buffer."""
+
+    def __init__(self, dim=256, depth=4):
+        super().__init__(dim, depth)
+        self.register_buffer("scale", torch.ones(dim))
+
+    def forward(self, x):
+        return super().forward(x) * self.scale
+
+
+def test_static_input_indices_reach_the_inference_compiler():
+    """Inside a dynamo compile the backend sees which graph inputs are the
+    module's lifted parameters and buffers (AOTAutograd's static inputs)."""
+    from torch._dynamo.backends.common import aot_autograd
+    from torch._functorch.aot_autograd import make_boxed_func
+
+    from compiler import backend as B
+
+    seen = []
+
+    def fw(gm, example_inputs):
+        seen.append((B._static_inputs(), len(example_inputs)))
+        return make_boxed_func(gm.forward)
+
+    model = _BlocksWithBuffer(dim=16, depth=1).eval()
+    torch._dynamo.reset()
+    with torch.no_grad():
+        torch.compile(model, backend=aot_autograd(fw_compiler=fw))(torch.randn(4, 16))
+    torch._dynamo.reset()
+    (static, n), = seen
+    assert len(static) == n - 1  # every input but x: 6 parameters and the buffer
+    assert B._static_inputs() == ()  # outside a compile
+
+
+@pytest.mark.gpu
+def test_replay_reads_buffers_in_place(monkeypatch):
+    """A module buffer is read from its own storage by the replay (not copied
+    into the graph per call): every input but x is recorded as read in
+    place, and an in-place change between calls is seen."""
+    from compiler.backend import custom_backend
+
+    recorded = []
+    orig = graph_replay.GraphReplay._record
+
+    def record(self, args):
+        orig(self, args)
+        recorded.append((self, len(args)))
+
+    monkeypatch.setattr(graph_replay.GraphReplay, "_record", record)
+    torch.manual_seed(2)
+    model = _BlocksWithBuffer().to(DEV, torch.bfloat16).eval()
+    x = torch.randn(256, 256, device=DEV, dtype=torch.bfloat16)
+    torch._dynamo.reset()
+    before = graph_replay.REPLAYS
+    with torch.no_grad():
+        f = torch.compile(model, backend=custom_backend)
+        for _ in range(3):
+            f(x)
+        model.scale.mul_(2.0)
+        got = f(x)
+        want = model(x)
+    torch._dynamo.reset()
+    assert graph_replay.REPLAYS - before >= 2
+    (r, n), = recorded
+    assert sum(r.persistent) == n - 1 and not r.persistent[[i for i in range(n) if i not in r.static][0]]
+    torch.testing.assert_close(got.float(), want.float(), rtol=5e-2, atol=5e-2)

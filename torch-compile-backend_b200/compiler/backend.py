@@ -128,8 +128,17 @@ def inference_compiler(gm: fx.GraphModule, example_inputs):
     gm = _passes(gm)
     fn = make_boxed_func(gm.forward)
     if config.EXTENSIONS:
-        fn = graph_replay.wrap(gm, fn)
+        fn = graph_replay.wrap(gm, fn, _static_inputs())
     return _checked(gm, example_inputs, fn)
+
+
+def _static_inputs() -> tuple:
+    """Indices of the graph inputs AOTAutograd marks static (the module's
+    parameters and buffers, lifted to inputs by dynamo); () outside a
+    dynamo compile."""
+    ctx = torch._guards.TracingContext.try_get()
+    meta = getattr(ctx, "fw_metadata", None) if ctx is not None else None
+    return tuple(getattr(meta, "static_input_indices", None) or ())
 
 
 custom_backend = aot_autograd(

@@ -75,12 +75,15 @@ def _is_persistent(t: torch.Tensor) -> bool:
 class GraphReplay:
     """Boxed callable: ``run(args)`` with ``args`` the graph's input list."""
 
-    def __init__(self, fn, no_clone=()):
+    def __init__(self, fn, no_clone=(), static=()):
         # AOTAutograd's marker for the list-argument calling convention (an
         # instance attribute, so that functools.wraps wrappers copy it)
         self._boxed_call = True
         self.fn = fn  # boxed op-by-op function of the compiled graph
         self.no_clone = frozenset(no_clone)  # output indices returned as the graph's own buffers
+        # input indices AOTAutograd marks static (the module's lifted parameters
+        # and buffers): read in place like parameters, guarded by their address
+        self.static = frozenset(static)
         self.calls = 0
         self.replays = 0
         self.graph = None
@@ -105,7 +108,8 @@ class GraphReplay:
             isinstance(a, (torch.Tensor, int, float, bool, type(None))) for a in args)
 
     def _record(self, args):
-        self.persistent = [isinstance(a, torch.Tensor) and _is_persistent(a) for a in args]
+        self.persistent = [isinstance(a, torch.Tensor) and (i in self.static or _is_persistent(a))
+                           for i, a in enumerate(args)]
         self.static_in = [a if (not isinstance(a, torch.Tensor) or p) else a.clone()
                           for a, p in zip(args, self.persistent)]
         self.sig = self._signature(args)
@@ -205,7 +209,7 @@ class TailReplay:
         return out
 
 
-def split_large_outputs(gm: fx.GraphModule):
+def split_large_outputs(gm: fx.GraphModule, static=()):
     """A TailReplay of `gm` whose tail computes the outputs larger than
     ``config.GRAPH_MAX_OUTPUT_MB``, or None when the graph does not split
     cleanly (a large output that is an input, a tail value that the body also
@@ -283,18 +287,19 @@ def split_large_outputs(gm: fx.GraphModule):
     tail_args = [("arg", placeholders.index(a)) if a.op == "placeholder" else ("body", len(small) + ext_body.index(a))
                  for a in ext]
     no_clone = range(len(small), len(small) + len(ext_body))
-    body = GraphReplay(lambda a: body_gm(*a), no_clone=no_clone)
+    body = GraphReplay(lambda a: body_gm(*a), no_clone=no_clone, static=static)
     return TailReplay(body, tail_gm, len(small), plan, tail_args)
 
 
-def wrap(gm: fx.GraphModule, boxed_fn):
+def wrap(gm: fx.GraphModule, boxed_fn, static=()):
     """The boxed function of an inference graph, replayed as a CUDA graph when
     it launches enough kernels to gain from it: whole when its outputs are
     small enough to clone per call, else split into a replayed body and a
-    tail run op by op (``split_large_outputs``); otherwise `boxed_fn`."""
+    tail run op by op (``split_large_outputs``); otherwise `boxed_fn`.
+    `static`: input indices read in place instead of copied per replay."""
     if not config.CUDA_GRAPHS or launching_nodes(gm) < config.GRAPH_MIN_LAUNCHES:
         return boxed_fn
     if output_bytes(gm) <= config.GRAPH_MAX_OUTPUT_MB * 2**20:
-        return GraphReplay(boxed_fn)
-    split = split_large_outputs(gm)
+        return GraphReplay(boxed_fn, static=static)
+    split = split_large_outputs(gm, static)
     return split if split is not None else boxed_fn
