@@ -246,7 +246,7 @@ def test_boxed_marker_survives_wrapping():
 class _BlocksWithBuffer(_Blocks):
     """_Blocks with a per-channel scale held as a module buffer."""
 
-    def __init__(self, dim=256, depth=4):
+    def __init__(self, dim=256, depth=6):
         super().__init__(dim, depth)
         self.register_buffer("scale", torch.ones(dim))
 
