@@ -256,6 +256,34 @@ typedef struct {
 int b200k_gemm_epilogue(const B200kGemmArgs* args, void* stream);
 
 /*
+ * Projection with the rotary position embedding as its epilogue:
+ *   out[m, :] = rope(round(a[m, :] @ b)) per 64-column head, with
+ *   rope(q)[d]      = round(round(q[d] cos[p][d]) - round(q[d + 32] sin[p][d]))
+ *   rope(q)[d + 32] = round(round(q[d + 32] cos[p][d + 32]) + round(q[d] sin[p][d + 32]))
+ * for d < 32 and p = m % period: x * cos + rotate_half(x) * sin with each
+ * product and the sum rounded to the 16-bit output type, as eager PyTorch
+ * computes it on the projection's 16-bit output.  Replaces the reference's
+ * plain mm (left to ATen, compiler/optimization/fusion_epilogue.py:45-69
+ * finds no pointwise anchor behind the view / transpose) followed by the
+ * rotation's separate kernels; not in the reference.
+ * args: as for b200k_gemm_epilogue with no extras and an empty program; a
+ * K-major in a, K-major b (t(W)), out of a/b's 16-bit type, N a multiple of
+ * 64, 16-byte aligned rows.  rope->cos / sin: [period, 64] tables of the
+ * output type, unit column stride, row stride `stride` elements (a multiple
+ * of 8), 16-byte aligned.  Runs the compiled epilogue on the 128 x 256,
+ * 128 x 128 or 256 x 256 (CTA pair) tiles.
+ */
+typedef struct {
+  const void* cos;
+  const void* sin;
+  int64_t stride;   /* elements between table rows */
+  int64_t period;   /* table rows; output row m uses row m % period */
+  int32_t head_dim; /* 64 */
+  int32_t dtype;    /* the tables' (= the output's) */
+} B200kRopeTables;
+int b200k_gemm_rope(const B200kGemmArgs* args, const B200kRopeTables* rope, void* stream);
+
+/*
  * b200k_gemm_epilogue for callers that cannot allocate device memory.
  * No reference counterpart: the reference has no allocation-free entry.
  * Hosts that run inside a graph-capture-only runtime, a plugin sandbox or a

@@ -112,10 +112,39 @@ STRUCTS = {
     "B200kSoftmaxArgs": (cabi.SoftmaxArgs, ["rows", "x", "log_softmax", "out", "out_dtype"]),
     "B200kRopeArgs": (cabi.RopeArgs, ["sizes", "x", "x_strides", "cos", "cos_strides", "sin", "sin_strides", "out",
                                       "out_strides", "dtype"]),
+    "B200kRopeTables": (cabi.RopeTables, ["cos", "sin", "stride", "period", "head_dim", "dtype"]),
     "B200kAttentionArgs": (cabi.AttentionArgs, ["batch", "head_dim", "q", "q_strides", "k", "k_strides", "v",
                                                 "v_strides", "out", "out_strides", "dtype", "causal", "scale",
                                                 "test_flags", "status", "timeout_ns"]),
 }
+
+
+def test_gemm_rope_host_checks():
+    """Argument errors of the rotary-epilogue GEMM, reported before any launch."""
+    lib = cabi.library()
+    g = cabi.GemmArgs()
+    g.M, g.N, g.K = 256, 512, 128
+    g.a, g.b, g.out = 4096, 8192, 16384
+    g.a_stride_m, g.a_stride_k, g.b_stride_k, g.b_stride_n = 128, 1, 1, 128
+    g.ab_dtype = g.out_dtype = cabi.BF16
+    r = cabi.RopeTables()
+    r.cos, r.sin, r.stride, r.period, r.head_dim, r.dtype = 32768, 65536, 64, 2048, 64, cabi.BF16
+    assert lib.b200k_gemm_rope(None, ctypes.byref(r), None) == 1
+    assert lib.b200k_gemm_rope(ctypes.byref(g), None, None) == 1
+    r.head_dim = 128
+    assert lib.b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), None) == 1  # 64-wide heads only
+    r.head_dim = 64
+    g.N = 520
+    assert lib.b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), None) == 3  # whole heads
+    g.N = 512
+    r.dtype = cabi.F16
+    assert lib.b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), None) == 4  # tables of the output type
+    r.dtype = cabi.BF16
+    r.stride = 60
+    assert lib.b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), None) == 2  # 16-byte table rows
+    r.stride = 64
+    g.n_extras = 1
+    assert lib.b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), None) == 1  # no other epilogue operands
 
 
 def test_attention_host_checks():

@@ -570,6 +570,45 @@ def test_rope_matches_eager_bit_for_bit(dtype, case):
     assert got.stride() == want.stride() and torch.equal(got, want)
 
 
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("B,S,H,K", [(2, 128, 4, 256), (3, 300, 8, 512), (8, 256, 32, 2048), (1, 2048, 8, 2048)])
+@pytest.mark.parametrize("config", [-1, 0, 1, 3])
+def test_gemm_rope_equals_gemm_then_rope(dtype, B, S, H, K, config):
+    """The rotary epilogue (b200k_gemm_rope) against the same GEMM stored
+    plainly and rotated by b200k_rope: bit-identical (the same accumulators
+    round to the same 16-bit q, and both rotations round each product and the
+    sum as eager PyTorch does); against eager PyTorch on the fp32 product
+    within one rounding; rows past a multiple of the period, partial tiles
+    (S = 300) and a padded table stride."""
+    dt = _tdt(dtype)
+    g = torch.Generator(device=DEV).manual_seed(B * 1000 + S + H)
+    N = H * 64
+    x = (0.5 * torch.randn(B * S, K, device=DEV, generator=g)).to(dt)
+    w = (0.05 * torch.randn(N, K, device=DEV, generator=g)).to(dt)
+    tab = torch.randn(2, S, 72, device=DEV, generator=g).to(dt)  # row stride 72 elements
+    cos, sin = tab[0, :, :64], tab[1, :, :64]
+    out = torch.empty(B * S, N, device=DEV, dtype=dt)
+    cabi.gemm_rope(x, w.t(), cos, sin, out, tile_config=config)
+    plain = torch.empty_like(out)
+    base_cfg = {3: 0, -1: cabi.library().b200k_gemm_pick_config(B * S, N, K)}.get(config, config)
+    base_cfg = {2: 0, 3: 0, 4: 0}.get(base_cfg, base_cfg)  # the same accumulators on one-CTA tiles
+    cabi.gemm_epilogue(x, w.t(), [], [], [], plain, tile_config=base_cfg)
+    q = plain.view(B, S, H, 64).transpose(1, 2)
+    want = torch.empty_strided(q.shape, q.stride(), device=DEV, dtype=dt)
+    cabi.rope(q, cos, sin, want)
+    torch.cuda.synchronize()
+    got = out.view(B, S, H, 64).transpose(1, 2)
+    assert torch.equal(got, want)
+    ref = _rope_eager((x.float() @ w.float().t()).to(dt).view(B, S, H, 64).transpose(1, 2), cos, sin)
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(),
+                               rtol=2e-2, atol=2e-2 * float(ref.float().abs().max()))
+    # the torch op, as the compiled graph calls it
+    op = torch.ops.b200.gemm_rope(x, w.t(), cos, sin, S, [B, S, N])
+    assert op.shape == (B, S, N)
+    if config == -1:  # the op picks the tile config as the C entry does by default
+        assert torch.equal(op.view(B * S, N), out)
+
+
 # ------------------------------------------------------------- failure detection
 @pytest.mark.parametrize("config", [0, 3, 4])
 def test_gemm_stalled_wait_times_out_and_context_survives(config):

@@ -98,7 +98,8 @@ def test_llama_small_bf16(attention_pass):
         got = torch.compile(model, backend=be)(ids)
     t = [str(s) for s in b200_targets(graphs)]
     assert "b200.rms_norm.default" in t
-    assert t.count("b200.rope.default") == 2 * 2  # q and k rotations per layer
+    assert t.count("b200.gemm_rope.default") == 2 * 2  # q and k projections with their rotations, per layer
+    assert "b200.rope.default" not in t
     assert t.count("b200.attention.default") == 2  # causal grouped-query attention per layer
     # per layer: o + residual, gate (silu * up), down + residual, all on the compiled path
     epi = [n for g in graphs for n in g.graph.nodes if n.op == "call_function"

@@ -385,7 +385,37 @@ def test_llama_layer_fuses_both_rotations():
     x = torch.randn(1, 16, 128).to(torch.bfloat16)
     cos, sin = m.cos[:16].to(torch.bfloat16), m.sin[:16].to(torch.bfloat16)
     graphs = fused_graphs(layer, (x, cos, sin))
+    # 32-wide heads: the rotations stay kernels of their own
     assert sum(len(_rope_nodes(g)) for g in graphs) == 2
+
+
+def test_rotated_projection_pass_rules():
+    """The q / k projection folds into gemm_rope only for a plain mm viewed
+    as 64-wide heads; a projection read by anything else, an fp32 one, or
+    extensions off keep the separate rotation (or no rotation kernel)."""
+    import bench_models as bm
+
+    def graph_of(layer, dt=torch.bfloat16, extensions=True):
+        m = bm.Llama(vocab=32, dim=256, layers=0, heads=4, kv_heads=2, ffn=256, max_seq=16)
+        x = torch.randn(2, 16, 256).to(dt)
+        cos, sin = m.cos[:16].to(dt), m.sin[:16].to(dt)
+        (gm,) = fused_graphs(layer.to(dt), (x, cos, sin), extensions=extensions)
+        return [str(n.target) for n in gm.graph.nodes if n.op == "call_function"]
+
+    class LeakQ(bm.LlamaLayer):
+        def forward(self, x, cos, sin):
+            B, S, _ = x.shape
+            q = self.q(self.in_norm(x)).view(B, S, self.h, self.hd).transpose(1, 2)
+            return q * cos + bm._rotate_half(q) * sin, q  # the unrotated heads escape
+
+    t = graph_of(bm.LlamaLayer(256, 4, 2, 256, 1e-5))
+    assert t.count("b200.gemm_rope.default") == 2 and "b200.rope.default" not in t
+    t = graph_of(LeakQ(256, 4, 2, 256, 1e-5))
+    assert "b200.gemm_rope.default" not in t and t.count("b200.rope.default") == 1
+    t = graph_of(bm.LlamaLayer(256, 4, 2, 256, 1e-5), extensions=False)
+    assert "b200.gemm_rope.default" not in t and "b200.rope.default" not in t
+    t = graph_of(bm.LlamaLayer(256, 4, 2, 256, 1e-5), dt=torch.float32)
+    assert "b200.gemm_rope.default" not in t
 
 
 class _Patch(nn.Module):

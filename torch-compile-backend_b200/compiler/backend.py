@@ -24,7 +24,7 @@ from compiler.optimization.fusion_attention import fuse_attention
 from compiler.optimization.fusion_epilogue import fuse_epilogue
 from compiler.optimization.fusion_patchify import fuse_patchify
 from compiler.optimization.fusion_pointwise import fuse_pointwise
-from compiler.optimization.fusion_rope import fuse_rope
+from compiler.optimization.fusion_rope import fuse_gemm_rope, fuse_rope
 from compiler.optimization.fusion_rowreduce import fuse_rowreduce
 
 runtime.load()
@@ -61,6 +61,8 @@ def _passes(gm: fx.GraphModule) -> fx.GraphModule:
     if config.EXTENSIONS and config.ENABLE_ROPE:
         gm = fuse_rope(gm)  # x*cos + rotate_half(x)*sin (extension; before the
         #                     pointwise pass would take its multiply-add)
+        if config.ENABLE_GEMM_ROPE:
+            gm = fuse_gemm_rope(gm)  # a rotated q / k projection -> one GEMM (extension)
     if config.ENABLE_EPILOGUE:
         gm = fuse_epilogue(gm)  # pointwise groups that consume a matmul
     if config.ENABLE_POINTWISE:

@@ -7,7 +7,9 @@ Environment flags (read once at import, overridable as module attributes):
   B200_EPILOGUE=0     skip the GEMM+epilogue pass
   B200_POINTWISE=0    skip the pointwise pass
   B200_ROWREDUCE=0    skip the row-reduction pass
-  B200_ROPE=0         skip the rotary-embedding pass
+  B200_ROPE=0         skip the rotary-embedding passes
+  B200_GEMM_ROPE=0    keep a rotated q / k projection as cuBLAS + the rotation
+                      kernel instead of one GEMM with the rotation epilogue
   B200_PATCHIFY=0     keep patch-embedding convolutions as convolutions
   B200_ATTENTION=1    replace ATen's scaled-dot-product attention nodes with
                       the library's attention kernel (off by default)
@@ -43,6 +45,7 @@ ENABLE_EPILOGUE = _flag("B200_EPILOGUE", True)
 ENABLE_POINTWISE = _flag("B200_POINTWISE", True)
 ENABLE_ROWREDUCE = _flag("B200_ROWREDUCE", True)
 ENABLE_ROPE = _flag("B200_ROPE", True)
+ENABLE_GEMM_ROPE = _flag("B200_GEMM_ROPE", True)
 ENABLE_PATCHIFY = _flag("B200_PATCHIFY", True)
 # The attention kernel is parity-tested but measured slower than PyTorch's
 # cuDNN SDPA on B200 (Llama-style prefill 327 vs 208 us, ViT-B/16 57 vs 35

@@ -152,3 +152,110 @@ def fuse_rope(gm: fx.GraphModule) -> fx.GraphModule:
     gm.graph.lint()
     gm.recompile()
     return gm
+
+
+# ---------------------------------------------------------------- projection
+# A rotation whose input is a projection viewed as heads,
+#
+#     mm(h, t(W)) -> [_unsafe_]view [B, S, H*64] -> view [B, S, H, 64]
+#       -> transpose(1, 2) -> b200.rope(., cos [S, 64], sin [S, 64])
+#
+# (a Llama-style q or k projection), becomes one GEMM with the rotation as its
+# epilogue, ``torch.ops.b200.gemm_rope`` (csrc/gemm_kernel.cuh, ROW_ROPE):
+# the projection's 16-bit product is rotated in registers before its only
+# store, so neither the product nor the rotation's input is written and read
+# back.  The reference leaves the projection to ATen (its anchor needs a
+# pointwise consumer, compiler/optimization/fusion_epilogue.py:45-69) and has
+# no rotation kernel.  Taken when the library's cost model predicts the fused
+# launch no slower than cuBLAS plus the rotation kernel.
+_VIEWS = (aten.view.default, aten._unsafe_view.default, aten.reshape.default)
+
+
+def _single_user(n: fx.Node) -> bool:
+    return len(n.users) == 1
+
+
+def _projection_of(x: fx.Node):
+    """(mm node, removed nodes, B, S, H) when x = transpose(view(...mm...), 1, 2)."""
+    if not (_is(x, aten.transpose.int) and _single_user(x) and tuple(x.args[1:]) in ((1, 2), (2, 1))):
+        return None
+    removed = [x]
+    n = x.args[0]
+    while isinstance(n, fx.Node) and any(_is(n, v) for v in _VIEWS) and _single_user(n):
+        removed.append(n)
+        n = n.args[0]
+    if not (isinstance(n, fx.Node) and _is(n, aten.mm.default) and _single_user(n) and len(removed) >= 2):
+        return None
+    v4 = _tensor_meta(removed[1])  # the [B, S, H, 64] view
+    if v4 is None or v4.dim() != 4:
+        return None
+    B, S, H, D = (int(d) for d in v4.shape)
+    return n, removed, B, S, H, D
+
+
+def _table2d(t: fx.Node, S: int):
+    """The [S, 64] table behind a cos / sin operand broadcast over batch and heads."""
+    v = _tensor_meta(t)
+    if v is None or v.dim() < 2 or tuple(v.shape[-2:]) != (S, 64) or any(d != 1 for d in v.shape[:-2]):
+        return None
+    if v.stride(-1) != 1 or v.stride(-2) % 8 or v.storage_offset() % 8:
+        return None
+    return v
+
+
+def fuse_gemm_rope(gm: fx.GraphModule) -> fx.GraphModule:
+    from .fusion_epilogue import fusion_pays
+
+    for node in list(gm.graph.nodes):
+        if node.graph is not gm.graph or not _is(node, torch.ops.b200.rope.default):
+            continue
+        x, cos, sin = node.args[:3]
+        proj = _projection_of(x) if isinstance(x, fx.Node) else None
+        if proj is None:
+            continue
+        mm, removed, B, S, H, D = proj
+        a, b = mm.args
+        av, bv, outv = _tensor_meta(a), _tensor_meta(b), _tensor_meta(node)
+        if av is None or bv is None or outv is None or D != 64:
+            continue
+        M, K = (int(d) for d in av.shape)
+        N = int(bv.shape[1])
+        if M != B * S or N != H * D or av.dtype not in (torch.bfloat16, torch.float16) or bv.dtype != av.dtype:
+            continue
+        if not (config.on_target_device(av) and config.on_target_device(bv)):
+            continue
+        if av.stride(1) != 1 or (av.stride(0) * 2) % 16 or bv.stride(0) != 1 or (bv.stride(1) * 2) % 16:
+            continue
+        if tuple(outv.stride()) != (S * N, D, N, 1):  # the rotation keeps the heads view of a row-major product
+            continue
+        cv, sv = _table2d(cos, S), _table2d(sin, S)
+        if cv is None or sv is None or cv.dtype != av.dtype or sv.dtype != av.dtype or cv.stride(-2) != sv.stride(-2):
+            continue
+        if not fusion_pays(M, N, K, 2, 2, 2 * S * 64 * 2):
+            continue
+        with gm.graph.inserting_before(node):
+            c2 = cos if cv.dim() == 2 else gm.graph.call_function(aten.view.default, (cos, [S, 64]))
+            s2 = sin if sv.dim() == 2 else gm.graph.call_function(aten.view.default, (sin, [S, 64]))
+            g = gm.graph.call_function(torch.ops.b200.gemm_rope.default, (a, b, c2, s2, S, [B, S, N]))
+            v = gm.graph.call_function(aten.view.default, (g, [B, S, H, D]))
+            t = gm.graph.call_function(aten.transpose.int, (v, 1, 2))
+        for n_new in (c2, s2):
+            if n_new is not cos and n_new is not sin:
+                n_new.meta["val"] = _tensor_meta(n_new.args[0]).view(S, 64)
+        g.meta["val"] = av.new_empty((B, S, N))
+        g.meta["b200_kernel"] = new_kernel_name("gemm_rope")
+        g.meta["b200_group"] = [str(mm.target), str(node.target)]
+        v.meta["val"] = g.meta["val"].view(B, S, H, D)
+        t.meta = dict(node.meta)
+        t.meta.pop("b200_kernel", None)
+        t.meta["val"] = v.meta["val"].transpose(1, 2)
+        node.replace_all_uses_with(t)
+        gm.graph.erase_node(node)
+        for n in removed:
+            if not n.users:
+                gm.graph.erase_node(n)
+        if not mm.users:
+            gm.graph.erase_node(mm)
+    gm.graph.lint()
+    gm.recompile()
+    return gm

@@ -87,6 +87,10 @@ def _register_fakes() -> None:
             return x.new_empty_strided(x.shape, out_stride)
         return x.new_empty(x.shape)
 
+    @torch.library.register_fake(lib + "gemm_rope")
+    def _(a, b, cos, sin, period, out_shape):
+        return a.new_empty(out_shape)
+
 
 def gemm_status(device: int = 0, reset: bool = True) -> int:
     """The GEMM kernels' device status word (0 = ok, 6 = a wait timed out);

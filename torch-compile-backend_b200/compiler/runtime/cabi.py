@@ -30,7 +30,7 @@ EXPORTED = [
     "b200k_pointwise", "b200k_gemm_epilogue", "b200k_gemm_num_configs", "b200k_gemm_config_info",
     "b200k_gemm_pick_config", "b200k_rownorm", "b200k_softmax", "b200k_status_string", "b200k_version",
     "b200k_gemm_epilogue_noalloc", "b200k_gemm_noalloc_status", "b200k_rope", "b200k_pointwise_jit_stats",
-    "b200k_pointwise_jit_compile", "b200k_attention",
+    "b200k_pointwise_jit_compile", "b200k_attention", "b200k_gemm_rope",
 ]
 
 
@@ -98,6 +98,11 @@ class RopeArgs(ctypes.Structure):
                 ("cos", ctypes.c_void_p), ("cos_strides", ctypes.c_int64 * 4), ("sin", ctypes.c_void_p),
                 ("sin_strides", ctypes.c_int64 * 4), ("out", ctypes.c_void_p), ("out_strides", ctypes.c_int64 * 4),
                 ("dtype", ctypes.c_int32), ("pad", ctypes.c_int32)]
+
+
+class RopeTables(ctypes.Structure):
+    _fields_ = [("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p), ("stride", ctypes.c_int64),
+                ("period", ctypes.c_int64), ("head_dim", ctypes.c_int32), ("dtype", ctypes.c_int32)]
 
 
 class AttentionArgs(ctypes.Structure):
@@ -249,6 +254,26 @@ def gemm_epilogue(a: torch.Tensor, b: torch.Tensor, extras: list[torch.Tensor], 
         _check("b200k_gemm_epilogue_noalloc", library().b200k_gemm_epilogue_noalloc(ctypes.byref(g), _stream()))
     else:
         _check("b200k_gemm_epilogue", library().b200k_gemm_epilogue(ctypes.byref(g), _stream()))
+
+
+def gemm_rope(a: torch.Tensor, b: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor,
+              tile_config: int = -1, status: torch.Tensor | None = None) -> None:
+    """out[M,N] = rope(round(a @ b)) per 64-column head, output row m rotated
+    by cos / sin row m % cos.shape[0] (b200k_gemm_rope)."""
+    g = GemmArgs()
+    M, K = a.shape
+    N = b.shape[1]
+    g.M, g.N, g.K = M, N, K
+    g.a, g.a_stride_m, g.a_stride_k = a.data_ptr(), a.stride(0), a.stride(1)
+    g.b, g.b_stride_k, g.b_stride_n = b.data_ptr(), b.stride(0), b.stride(1)
+    g.ab_dtype = g.out_dtype = DTYPE[a.dtype]
+    g.out, g.out_stride_m, g.out_stride_n = out.data_ptr(), out.stride(0), out.stride(1)
+    g.tile_config = tile_config
+    g.status = status.data_ptr() if status is not None else None
+    r = RopeTables()
+    r.cos, r.sin, r.stride, r.period = cos.data_ptr(), sin.data_ptr(), cos.stride(0), cos.shape[0]
+    r.head_dim, r.dtype = cos.shape[1], DTYPE[cos.dtype]
+    _check("b200k_gemm_rope", library().b200k_gemm_rope(ctypes.byref(g), ctypes.byref(r), _stream()))
 
 
 def gemm_noalloc_status() -> int:

@@ -37,6 +37,9 @@ int B200K_PAIR_FN(B200K_FAST_ACT)(int row, const CUtensorMap& ta, const CUtensor
     case ROW_RES: return launch_pair<kStages, 2, kAct, ROW_RES, kWide>(ta, tb, to, p, grid, st);
     case ROW_SCALE_PK: return launch_pair<kStages, 2, kAct, ROW_SCALE_PK, kWide>(ta, tb, to, p, grid, st);
     case ROW_RES_PK: return launch_pair<kStages, 2, kAct, ROW_RES_PK, kWide>(ta, tb, to, p, grid, st);
+#if B200K_FAST_ACT == 0 && B200K_FAST_BN == 2
+    case ROW_ROPE: return launch_pair<kStages, 2, kAct, ROW_ROPE, false>(ta, tb, to, p, grid, st);
+#endif
     default: return B200K_ERR_UNSUPPORTED;
   }
 }
@@ -62,6 +65,12 @@ int launch_row16(int row, const CUtensorMap& ta, const CUtensorMap& tb, const CU
     case ROW_RES: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_RES>(ta, tb, to, p, grid, st);
     case ROW_SCALE_PK: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_SCALE_PK>(ta, tb, to, p, grid, st);
     case ROW_RES_PK: return launch_one<kBN, kStages, BNM, 2, true, kAct, ROW_RES_PK>(ta, tb, to, p, grid, st);
+#if B200K_FAST_ACT == 0 && B200K_FAST_BN != 192
+    // the rotary-embedding epilogue (K-major B; eight epilogue warps)
+    case ROW_ROPE:
+      if (BNM) return B200K_ERR_UNSUPPORTED;
+      return launch_one<kBN, kStages, false, 2, true, kAct, ROW_ROPE>(ta, tb, to, p, grid, st);
+#endif
     default: return B200K_ERR_UNSUPPORTED;
   }
 }

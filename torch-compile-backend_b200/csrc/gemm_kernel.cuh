@@ -108,6 +108,12 @@ struct Params {
   int32_t bias_dt;
   const void* row_ptr;
   int64_t row_sm;
+  // ROW_ROPE: rotary tables [period, 64] of the output type, row stride in
+  // elements; output row m takes table row m % period
+  const void* rope_cos;
+  const void* rope_sin;
+  int64_t rope_stride;
+  int32_t rope_period;
   unsigned long long* trace;                       // diagnostic timeline, null = off
   EpiOperand ex[B200K_MAX_INPUTS - 1];
   B200kProgram prog;
@@ -576,7 +582,7 @@ enum { XM_NONE = 0, XM_BCAST = 1, XM_ROW16 = 2, XM_GENERIC = 3 };
 //                of an 8- or 11-bit-significand type is exact in fp32, so the
 //                packed op's single rounding equals fp32-then-round, the
 //                decomposed graph's order.
-enum { ROW_NONE = 0, ROW_SCALE = 1, ROW_RES = 2, ROW_SCALE_PK = 3, ROW_RES_PK = 4 };
+enum { ROW_NONE = 0, ROW_SCALE = 1, ROW_RES = 2, ROW_SCALE_PK = 3, ROW_RES_PK = 4, ROW_ROPE = 5 };
 
 struct FastOps {
   uint4 row_r[4];  // the full-matrix operand's 32 values of this lane's row
@@ -819,6 +825,134 @@ __device__ __forceinline__ void fast_sub_chunk(const Params& p, const CUtensorMa
   }
 }
 
+// ------------------------------------------------- rotary-embedding epilogue
+// ROW_ROPE: the output is the projection q = round(acc) (16-bit) rotated as
+//   out[d]      = round(round(q[d] cos[d])           - round(q[d + 32] sin[d]))
+//   out[d + 32] = round(round(q[d + 32] cos[d + 32]) + round(q[d] sin[d + 32]))
+// for each 64-column head (d < 32), with cos / sin the row's table entries:
+// x cos + rotate_half(x) sin with every product and the sum rounded to the
+// 16-bit type, as eager PyTorch computes it (a product or sum of two 16-bit
+// values is exact in fp32, so the packed bf16x2 / f16x2 ops round exactly
+// once, as the fp32-then-round of eager does).  A warp's step covers one head
+// of its 32 rows: two 32-column accumulator loads, one 128-byte staging row,
+// one TMA store.  The row's 64 cos and 64 sin values are loaded once per tile,
+// before the accumulator wait.
+__device__ __forceinline__ uint32_t pk_sub(uint32_t a, uint32_t b, bool bf16) {
+  uint32_t d;
+  if (bf16) asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+__device__ __forceinline__ void load_rope_row(const Params& p, int m, uint4 (&cs)[16]) {
+  const int64_t off = static_cast<int64_t>(m % p.rope_period) * p.rope_stride;
+  const uint4* c = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.rope_cos) + off);
+  const uint4* sn = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(p.rope_sin) + off);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    cs[i] = __ldg(c + i);
+    cs[8 + i] = __ldg(sn + i);
+  }
+}
+
+__device__ __forceinline__ void tmem_wait_ld_regs2(uint32_t (&a)[32], uint32_t (&b)[32]) {
+  tmem_wait_ld_regs(a);
+  // orders every use of b after the wait as well (volatile asm statements keep their order)
+  asm volatile(""
+               : "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+                 "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]),
+                 "+r"(b[15]), "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]),
+                 "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]),
+                 "+r"(b[29]), "+r"(b[30]), "+r"(b[31])
+               :
+               : "memory");
+}
+
+// 32 accumulator values of a row rounded to the 16-bit output type, packed in pairs.
+__device__ __forceinline__ void round_pack32(const uint32_t (&raw)[32], bool bf16, uint32_t (&q)[16]) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(raw[8 * g + j]);
+    const uint4 u = bf16 ? pack_bf16x8(v) : pack_f16x8(v);
+    q[4 * g] = u.x;
+    q[4 * g + 1] = u.y;
+    q[4 * g + 2] = u.z;
+    q[4 * g + 3] = u.w;
+  }
+}
+
+template <int BN, bool PAIR>
+__device__ __forceinline__ void epilogue_rope_loop(const Params& p, const CUtensorMap* tmO, uint32_t tmem_base,
+                                                   uint64_t* tfull, uint64_t* tempty, uint8_t* sb, int quarter,
+                                                   int cg, int lane, const Ctl& ctl, uint32_t rank) {
+  constexpr int CW = Epi<BN>::CW;
+  static_assert(CW % 64 == 0, "whole heads per warp");
+  constexpr int TM = PAIR ? 2 * BM : BM;
+  const int t0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
+  const int rank_rows = static_cast<int>(rank) * BM;
+  const bool bf16 = p.out_dt == B200K_BF16;
+  int acc = 0;
+  uint32_t aph = 0;
+  for (int t = t0; t < p.num_tiles; t += step) {
+    int tm, tn;
+    tile_coords(t, p, tm, tn);
+    const int row0 = tm * TM + rank_rows + quarter * 32;
+    uint4 cs[16];  // cos[0:64] in cs[0..7], sin[0:64] in cs[8..15]
+    load_rope_row(p, row0 + lane, cs);
+    if (!wait_bar(&tfull[acc], aph, ctl)) break;
+    tc_fence_after();
+    const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                           static_cast<uint32_t>(acc * BN + cg * CW);
+#pragma unroll 1
+    for (int h = 0; h < CW / 64; ++h) {
+      const int n = tn * BN + cg * CW + h * 64;
+      if (n >= p.N) break;  // warp-uniform; N is a multiple of 64
+      uint32_t a0[32], a1[32];
+      tmem_ld32(t_row + h * 64, a0);
+      tmem_ld32(t_row + h * 64 + 32, a1);
+      tmem_wait_ld_regs2(a0, a1);
+      uint32_t q0[16], q1[16];
+      round_pack32(a0, bf16, q0);
+      round_pack32(a1, bf16, q1);
+      const uint32_t* c = reinterpret_cast<const uint32_t*>(cs);  // c[0..31] cos, c[32..63] sin (bf16x2)
+      uint32_t o[32];
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        o[k] = pk_sub(pk_op(q0[k], c[k], bf16, true), pk_op(q1[k], c[32 + k], bf16, true), bf16);
+        o[16 + k] = pk_op(pk_op(q1[k], c[16 + k], bf16, true), pk_op(q0[k], c[48 + k], bf16, true), bf16, false);
+      }
+      // the previous store has read the staging row
+      if (lane == 0) bulk_wait_read_all();
+      __syncwarp();
+#pragma unroll
+      for (int g = 0; g < 8; ++g)
+        *reinterpret_cast<uint4*>(sb + lane * 128 + ((g ^ (lane & 7)) << 4)) =
+            make_uint4(o[4 * g], o[4 * g + 1], o[4 * g + 2], o[4 * g + 3]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tmO, sb, n, row0);
+        bulk_commit();
+      }
+    }
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) {
+      if (PAIR && rank != 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+      else mbar_arrive(&tempty[acc]);
+    }
+    if (++acc == 2) {
+      acc = 0;
+      aph ^= 1u;
+    }
+  }
+  if (lane == 0) bulk_wait_all();
+  __syncwarp();
+}
+
 // PAIR: the tiles are 256 rows high, one per CTA pair (the grid's cluster
 // index walks them), and this CTA's 128 rows start at `rank` x 128; the
 // accumulator is released on the even CTA's barrier.
@@ -833,6 +967,11 @@ __device__ __forceinline__ void epilogue_fast_loop(const Params& p, const CUtens
                                                    int quarter, int cg, int lane, const Ctl& ctl,
                                                    uint32_t rank = 0) {
   static_assert(PAIR || !WIDE, "wide tiles run on CTA pairs");
+  if constexpr (ROW == ROW_ROPE) {
+    static_assert(!WIDE && OUT_BYTES == 2 && ACT == B200K_ACT_NONE, "rotary epilogue: narrow tiles, 16-bit output");
+    epilogue_rope_loop<BN, PAIR>(p, tmO, tmem_base, tfull, tempty, sb, quarter, cg, lane, ctl, rank);
+    return;
+  }
   constexpr int CW = Epi<BN>::CW;
   constexpr int NSUB = CW / 32;  // 32-column sub-chunks per warp and accumulator half
   constexpr int TM = PAIR ? 2 * BM : BM;  // rows per tile

@@ -285,7 +285,26 @@ extern "C" int b200k_gemm_pick_config(int64_t M, int64_t N, int64_t K) {
   return pick(M, N, K, sms, true, true);
 }
 
-extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
+namespace {
+int gemm_run(const B200kGemmArgs* a, const B200kRopeTables* rope, void* stream_);
+}  // namespace
+
+extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) { return gemm_run(a, nullptr, stream_); }
+
+extern "C" int b200k_gemm_rope(const B200kGemmArgs* a, const B200kRopeTables* r, void* stream_) {
+  if (!a || !r) return B200K_ERR_ARG;
+  if (a->n_extras != 0 || a->program.n != 0) return B200K_ERR_ARG;
+  if (r->head_dim != 64 || r->period <= 0 || r->period > 0x7fffffff || !r->cos || !r->sin) return B200K_ERR_ARG;
+  if (a->ab_dtype != B200K_BF16 && a->ab_dtype != B200K_F16) return B200K_ERR_UNSUPPORTED;
+  if (a->out_dtype != a->ab_dtype || r->dtype != a->out_dtype) return B200K_ERR_UNSUPPORTED;
+  if (a->N % 64 != 0) return B200K_ERR_SHAPE;
+  if (!aligned16(r->cos) || !aligned16(r->sin) || r->stride % 8 != 0) return B200K_ERR_ALIGN;
+  if (a->b_stride_k != 1 || (a->a_stride_k != 1 && a->K > 1)) return B200K_ERR_UNSUPPORTED;
+  return gemm_run(a, r, stream_);
+}
+
+namespace {
+int gemm_run(const B200kGemmArgs* a, const B200kRopeTables* rope, void* stream_) {
   if (!a) return B200K_ERR_ARG;
   if (a->M < 0 || a->N < 0 || a->K < 0) return B200K_ERR_SHAPE;
   if (a->M == 0 || a->N == 0) return B200K_OK;  // empty output: nothing to launch
@@ -360,8 +379,10 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   const bool row_ok = role_idx < 0 || (ob == 2 && mode_of(role_idx, true) == XM_ROW16 &&
                                        a->extras[role_idx].dtype == a->out_dtype);
   const int bias_mode = mode_of(a->form.bias, false);
-  const bool fast = a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) && !amm &&
-                    (bias_mode == XM_NONE || bias_mode == XM_BCAST);
+  const bool fast = rope ? tma_out
+                         : a->form.kind == 1 && tma_out && act_ok && !both && row_ok && !(bnm && ob == 4) && !amm &&
+                               (bias_mode == XM_NONE || bias_mode == XM_BCAST);
+  if (rope && !fast) return B200K_ERR_ALIGN;  // the rotary epilogue stores with TMA only
 
   const bool pair_ok = fast && !bnm && ob == 2 && !tf32;  // the CTA-pair kernels' domain
 
@@ -372,6 +393,8 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (cfg >= kNumConfigs) return B200K_ERR_ARG;
   if (kConfigs[cfg].bn == 192 && (!fast || tf32)) cfg = 0;  // 192-wide tiles: compiled 16-bit epilogues only
   if (kConfigs[cfg].bm == 2 * BM && !pair_ok) cfg = 0;
+  if (rope && kConfigs[cfg].bn == 192) cfg = 0;  // the rotary epilogue runs on eight-warp tiles
+  if (rope && kConfigs[cfg].bn == 2 * kPairMmaN) cfg = 3;  // and on narrow pair tiles
   const int bn = kConfigs[cfg].bn;
   const int bm = kConfigs[cfg].bm;
   const bool pair = bm == 2 * BM;
@@ -455,6 +478,15 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (a->trace && a->trace_words >= static_cast<int64_t>(grid) * B200K_GEMM_TRACE_WORDS)
     p.trace = reinterpret_cast<unsigned long long*>(a->trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream_);
+  if (rope) {
+    p.f_bias = -1;
+    p.rope_cos = rope->cos;
+    p.rope_sin = rope->sin;
+    p.rope_stride = rope->stride;
+    p.rope_period = static_cast<int32_t>(rope->period);
+    if (pair) return launch_pair(false, B200K_ACT_NONE, ROW_ROPE, ta, tb, to, p, grid, st);
+    return launch_fast(bn, B200K_ACT_NONE, false, false, ob, ROW_ROPE, ta, tb, to, p, grid, st);
+  }
   if (fast) {
     int row = ROW_NONE;
     if (role_idx >= 0) {
@@ -475,6 +507,7 @@ extern "C" int b200k_gemm_epilogue(const B200kGemmArgs* a, void* stream_) {
   if (cfg == 0 || bn == 192) return launch_interp<256, 4>(tf32, amm, bnm, ob, ta, tb, to, p, grid, st);
   return launch_interp<128, 6>(tf32, amm, bnm, ob, ta, tb, to, p, grid, st);
 }
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // Allocation-free entry (see b200k.h): the status word lives in this

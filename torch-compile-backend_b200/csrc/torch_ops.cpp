@@ -207,6 +207,56 @@ at::Tensor gemm_epilogue(const at::Tensor& a, const at::Tensor& b, at::TensorLis
   return out;
 }
 
+// out [M, N] = rope(round(a @ b)) per 64-column head with the rotary tables
+// cos / sin [period, 64] (b200k_gemm_rope); out_shape as for gemm_epilogue.
+at::Tensor gemm_rope(const at::Tensor& a, const at::Tensor& b, const at::Tensor& cos, const at::Tensor& sin,
+                     int64_t period, at::IntArrayRef out_shape) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && cos.is_cuda() && sin.is_cuda(), "b200::gemm_rope: CUDA tensors only");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(0), "b200::gemm_rope: a [M,K], b [K,N]");
+  TORCH_CHECK(cos.dim() == 2 && sin.dim() == 2 && cos.size(0) == period && sin.size(0) == period &&
+                  cos.size(1) == 64 && sin.size(1) == 64 && cos.stride(1) == 1 && sin.stride(1) == 1 &&
+                  cos.stride(0) == sin.stride(0),
+              "b200::gemm_rope: cos / sin must be [period, 64] tables with unit column stride");
+  TORCH_CHECK(a.scalar_type() == b.scalar_type() && cos.scalar_type() == a.scalar_type() &&
+                  sin.scalar_type() == a.scalar_type(),
+              "b200::gemm_rope: a, b, cos, sin must share one 16-bit dtype");
+  const int64_t M = a.size(0), K = a.size(1), N = b.size(1);
+  int64_t numel = 1;
+  for (auto s : out_shape) numel *= s;
+  TORCH_CHECK(numel == M * N && !out_shape.empty(), "b200::gemm_rope: out_shape ", out_shape, " does not hold [", M,
+              ", ", N, "]");
+  c10::cuda::CUDAGuard guard(a.device());
+  at::Tensor out = at::empty(out_shape, a.options());
+  B200kGemmArgs g;
+  std::memset(&g, 0, sizeof(g));
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.a = a.data_ptr();
+  g.a_stride_m = a.stride(0);
+  g.a_stride_k = a.stride(1);
+  g.b = b.data_ptr();
+  g.b_stride_k = b.stride(0);
+  g.b_stride_n = b.stride(1);
+  g.ab_dtype = to_dt(a.scalar_type());
+  g.out_dtype = g.ab_dtype;
+  g.out = out.data_ptr();
+  g.out_stride_m = N;
+  g.out_stride_n = 1;
+  g.tile_config = -1;
+  g.status = status_word(a.device().index()).data_ptr<int32_t>();
+  B200kRopeTables r;
+  std::memset(&r, 0, sizeof(r));
+  r.cos = cos.data_ptr();
+  r.sin = sin.data_ptr();
+  r.stride = cos.stride(0);
+  r.period = period;
+  r.head_dim = 64;
+  r.dtype = g.ab_dtype;
+  check(b200k_gemm_rope(&g, &r, stream_of(a)), "gemm_rope");
+  return out;
+}
+
 int64_t gemm_status(int64_t device, bool reset) {
   at::Tensor& w = status_word(static_cast<int>(device));
   const int64_t v = w.item<int32_t>();
@@ -506,6 +556,7 @@ TORCH_LIBRARY(b200, m) {
   m.def("softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("log_softmax(Tensor x, int dim, bool half_to_float) -> Tensor");
   m.def("rope(Tensor x, Tensor cos, Tensor sin, int[] out_stride=[]) -> Tensor");
+  m.def("gemm_rope(Tensor a, Tensor b, Tensor cos, Tensor sin, int period, int[] out_shape) -> Tensor");
   m.def("attention(Tensor q, Tensor k, Tensor v, bool causal, float scale, int[] out_stride=[]) -> Tensor");
   m.def("gemm_status(int device, bool reset) -> int", &gemm_status);
   m.def("status_check(int device, bool arm) -> int", &status_check);
@@ -521,6 +572,7 @@ TORCH_LIBRARY_IMPL(b200, CUDA, m) {
   m.impl("softmax", &softmax);
   m.impl("log_softmax", &log_softmax);
   m.impl("rope", &rope);
+  m.impl("gemm_rope", &gemm_rope);
   m.impl("attention", &attention);
 }
 
