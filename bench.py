@@ -262,6 +262,7 @@ def run_sweep(args, dist: Dist) -> dict:
     def step(record=None):
         for j, p in enumerate(probs):
             if record is not None:
+                _gpu_lead()  # the events then bracket the kernel, not the host's enqueue
                 record[j][0].record()
             out = p["call"]()
             if record is not None:
@@ -392,6 +393,8 @@ def run_sweep(args, dist: Dist) -> dict:
         "config": {"workload": "gemm_epilogue_sweep", "shapes": SWEEP, "acts": ACTS,
                    "epilogue": "act(X W^T + b) + R, bf16 in/out, fp32 accumulate",
                    "l2": "256 MB flush between steps (outside the per-launch events)",
+                   "timing": "CUDA events per launch, each after a ~100 us GPU spin (outside the events) so "
+                             "the host's enqueue is not timed",
                    "parallelism": f"replicas x{n}"},
         "roofline": {"bound": "tensor", "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(achieved / peak, 3), "peak_source": f"{src} bf16_tflops (burst)",
@@ -448,7 +451,8 @@ def run_sweep_backend(args, dist: Dist) -> dict:
             f(x, r)
         torch.cuda.synchronize()
         compile_s = time.perf_counter() - t0
-        per = [_time_device(lambda f=f, x=x, r=r: f(x, r), args.steps, args.warmup, flush) for f, x, r in calls]
+        per = [_time_device(lambda f=f, x=x, r=r: f(x, r), args.steps, args.warmup, flush, lead=True)
+               for f, x, r in calls]
     total_ms = sum(statistics.median(t) for t in per)
     return {"metric": "fused GEMM+epilogue TFLOP/s", "value": round(flops / (total_ms * 1e-3) / 1e12, 2),
             "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
@@ -569,11 +573,24 @@ def _backend(name: str):
     raise ValueError(name)
 
 
-def _time_device(fn, steps: int, warmup: int, flush=None) -> list[float]:
+LEAD_CYCLES = 200_000  # ~100 us of GPU spin at the B200's 1965 MHz
+
+
+def _gpu_lead() -> None:
+    """Queues a short GPU spin outside the timed events: while it runs the
+    host enqueues the start event, the launch and the end event, so a
+    launch whose host-side cost exceeds its kernel time (512^3) is timed as
+    the kernel, not as the host's enqueue.  Both sweep legs (this library and
+    the backends compared with it) use it."""
+    torch.cuda._sleep(LEAD_CYCLES)
+
+
+def _time_device(fn, steps: int, warmup: int, flush=None, lead: bool = False) -> list[float]:
     """Device time of each of `steps` calls (CUDA events on the current
     stream around the call, an L2 flush between calls).  The steps are queued
     back to back and synchronised once at the end, so the host's per-call
-    cost overlaps the device's work, as in a running model."""
+    cost overlaps the device's work, as in a running model; with `lead`, a
+    GPU spin before each call keeps the host's enqueue out of the events."""
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -581,6 +598,8 @@ def _time_device(fn, steps: int, warmup: int, flush=None) -> list[float]:
     for _ in range(steps):
         if flush is not None:
             flush.zero_()
+        if lead:
+            _gpu_lead()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         fn()
