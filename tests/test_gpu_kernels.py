@@ -571,7 +571,8 @@ def test_rope_matches_eager_bit_for_bit(dtype, case):
 
 
 @pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
-@pytest.mark.parametrize("B,S,H,K", [(2, 128, 4, 256), (3, 300, 8, 512), (8, 256, 32, 2048), (1, 2048, 8, 2048)])
+@pytest.mark.parametrize("B,S,H,K", [(2, 128, 4, 256), (3, 300, 8, 512), (8, 256, 32, 2048), (1, 2048, 8, 2048),
+                                     (8, 2048, 32, 2048)])
 @pytest.mark.parametrize("config", [-1, 0, 1, 3])
 def test_gemm_rope_equals_gemm_then_rope(dtype, B, S, H, K, config):
     """The rotary epilogue (b200k_gemm_rope) against the same GEMM stored
