@@ -389,6 +389,30 @@ def test_llama_layer_fuses_both_rotations():
     assert sum(len(_rope_nodes(g)) for g in graphs) == 2
 
 
+def test_rotated_projection_with_broadcast_tables():
+    """cos / sin given as [1, 1, S, 64] tables (the Hugging Face layout) are
+    viewed as [S, 64] for the rotary GEMM."""
+    import bench_models as bm
+
+    class HFStyle(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.q = nn.Linear(256, 256, bias=False)
+
+        def forward(self, x, cos, sin):
+            B, S, _ = x.shape
+            q = self.q(x).view(B, S, 4, 64).transpose(1, 2)
+            return q * cos + bm._rotate_half(q) * sin
+
+    m = bm.Llama(vocab=32, dim=256, layers=0, heads=4, kv_heads=2, ffn=256, max_seq=16)
+    cos, sin = (t[:16].to(torch.bfloat16)[None, None] for t in (m.cos, m.sin))
+    (gm,) = fused_graphs(HFStyle().to(torch.bfloat16), (torch.randn(2, 16, 256).to(torch.bfloat16), cos, sin))
+    (node,) = [n for n in gm.graph.nodes if n.op == "call_function" and n.target == torch.ops.b200.gemm_rope.default]
+    for t in node.args[2:4]:
+        assert tuple(t.meta["val"].shape) == (16, 64)
+    assert node.args[4] == 16 and tuple(node.meta["val"].shape) == (2, 16, 256)
+
+
 def test_rotated_projection_pass_rules():
     """The q / k projection folds into gemm_rope only for a plain mm viewed
     as 64-wide heads; a projection read by anything else, an fp32 one, or
