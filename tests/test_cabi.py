@@ -198,3 +198,14 @@ def test_ctypes_layout_matches_c():
         cls = STRUCTS[cname][0]
         got = ctypes.sizeof(cls) if field == "size" else getattr(cls, field).offset
         assert got == int(value), f"{cname}.{field}: ctypes {got} vs C {value}"
+
+
+def test_missing_library_fails_loudly(monkeypatch):
+    """Without the built extension the runtime raises instead of falling back
+    to anything: there is no CPU or eager path inside the compiled graph."""
+    from compiler import runtime
+
+    monkeypatch.setattr(runtime, "_loaded", False)
+    monkeypatch.setattr(runtime, "EXT_PATH", "/nonexistent/_b200_ops.so")
+    with pytest.raises(runtime.LibraryMissing):
+        runtime.load()
